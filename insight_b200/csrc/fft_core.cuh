@@ -1,0 +1,308 @@
+// fft_core.cuh — register/shared-memory Stockham FFT building blocks for the
+// fused spectral kernels (sm_100a).
+//
+// A transform of length L is computed by one "group" of P threads.  Each
+// thread keeps E = L / P complex values in registers.  The transform runs as
+// a sequence of Stockham autosort passes (radix R_p = min(E, L / Ns_p), Ns the
+// product of the previous radices).  Pass p, butterfly j (0 <= j < L/R):
+//     k    = j mod Ns
+//     a[r] = data[j + r*L/R] * W_{Ns*R}^{r*k}          r = 0..R-1
+//     A    = DFT_R(a)                                 (in registers)
+//     data'[(j/Ns)*Ns*R + k + r*Ns] = A[r]
+// with W_N = exp(-2*pi*i/N) (the forward, unnormalised DFT that FFTW_FORWARD
+// and numpy.fft.fft compute).  After the last pass data' is the DFT in
+// natural order.  Between passes the values go through a padded shared-memory
+// buffer (one pad slot every 16 values keeps the strided writes of the first
+// pass bank-conflict free).  Each thread owns B = E/R butterflies per pass,
+// j = t + b*P.  The R-point DFTs are radix-2 decimation-in-frequency networks
+// unrolled at compile time; their twiddles are compile-time constants
+// (cos(2*pi*m/32), m = 0..31, R <= 32).  Stockham twiddles W_{Ns*R}^{r*k}
+// are formed per butterfly from one table value W_{Ns*R}^k by binary
+// splitting (W^r = W^{r/2} * W^{r-r/2}), so each power is at most log2(R)
+// rounded products away from the table value.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <type_traits>
+
+namespace ib200 {
+
+template <typename T> struct V2T;
+template <> struct V2T<float> { using type = float2; };
+template <> struct V2T<double> { using type = double2; };
+
+template <typename V> __device__ __forceinline__ V vadd(V a, V b) {
+  return {a.x + b.x, a.y + b.y};
+}
+template <typename V> __device__ __forceinline__ V vsub(V a, V b) {
+  return {a.x - b.x, a.y - b.y};
+}
+// a * b (complex)
+template <typename V> __device__ __forceinline__ V vmul(V a, V b) {
+  return {fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x)};
+}
+// conj(a) * b
+template <typename V> __device__ __forceinline__ V vcmul(V a, V b) {
+  return {fma(a.x, b.x, a.y * b.y), fma(a.x, b.y, -a.y * b.x)};
+}
+
+// cos(2*pi*m/32) for m in [0, 32).
+__host__ __device__ constexpr double cos32(int m) {
+  switch (m & 31) {
+  case 0: return 1.0;
+  case 1: return 0.98078528040323043;
+  case 2: return 0.92387953251128674;
+  case 3: return 0.83146961230254524;
+  case 4: return 0.70710678118654757;
+  case 5: return 0.55557023301960229;
+  case 6: return 0.38268343236508984;
+  case 7: return 0.19509032201612833;
+  case 8: return 0.0;
+  case 9: return -0.19509032201612833;
+  case 10: return -0.38268343236508984;
+  case 11: return -0.55557023301960229;
+  case 12: return -0.70710678118654757;
+  case 13: return -0.83146961230254524;
+  case 14: return -0.92387953251128674;
+  case 15: return -0.98078528040323043;
+  case 16: return -1.0;
+  case 17: return -0.98078528040323043;
+  case 18: return -0.92387953251128674;
+  case 19: return -0.83146961230254524;
+  case 20: return -0.70710678118654757;
+  case 21: return -0.55557023301960229;
+  case 22: return -0.38268343236508984;
+  case 23: return -0.19509032201612833;
+  case 24: return 0.0;
+  case 25: return 0.19509032201612833;
+  case 26: return 0.38268343236508984;
+  case 27: return 0.55557023301960229;
+  case 28: return 0.70710678118654757;
+  case 29: return 0.83146961230254524;
+  case 30: return 0.92387953251128674;
+  default: return 0.98078528040323043;
+  }
+}
+
+// v * W_32^Q, W_32 = exp(-2*pi*i/32).  Multiples of a quarter turn are exact.
+template <typename T, int Q, typename V>
+__device__ __forceinline__ V mul_w32(V v) {
+  constexpr int q = Q & 31;
+  if constexpr (q == 0) {
+    return v;
+  } else if constexpr (q == 8) {
+    return {v.y, -v.x};
+  } else if constexpr (q == 16) {
+    return {-v.x, -v.y};
+  } else if constexpr (q == 24) {
+    return {-v.y, v.x};
+  } else {
+    constexpr T c = (T)cos32(q);
+    constexpr T s = (T)cos32(q + 24); // sin(2*pi*q/32)
+    // (x + iy)(c - is) = (xc + ys) + i(yc - xs)
+    return {fma(v.x, c, v.y * s), fma(v.y, c, -(v.x * s))};
+  }
+}
+
+template <int I> using IC = std::integral_constant<int, I>;
+
+template <int B, int E, int S = 1, typename F>
+__device__ __forceinline__ void static_for(F &&f) {
+  if constexpr (B < E) {
+    f(IC<B>{});
+    static_for<B + S, E, S>(f);
+  }
+}
+
+template <int R> __host__ __device__ constexpr int bitrev(int v) {
+  int r = 0;
+  for (int m = R >> 1, b = 1; m >= 1; m >>= 1, b <<= 1)
+    if (v & m)
+      r |= b;
+  return r;
+}
+
+// In-register R-point forward DFT, natural order in and out.
+template <typename T, int R, typename V>
+__device__ __forceinline__ void dft_reg(V *a) {
+  static_assert(R >= 1 && R <= 32 && (R & (R - 1)) == 0, "radix");
+  if constexpr (R > 1) {
+    // radix-2 DIF network: span H = R/2, R/4, ..., 1
+    static_for<0, 32>([&](auto sIC) {
+      constexpr int s = decltype(sIC)::value;
+      constexpr int H = R >> (s + 1);
+      if constexpr (H >= 1) {
+        static_for<0, R, 2 * H>([&](auto bIC) {
+          constexpr int blk = decltype(bIC)::value;
+          static_for<0, H>([&](auto iIC) {
+            constexpr int i = decltype(iIC)::value;
+            V u = a[blk + i], w = a[blk + i + H];
+            a[blk + i] = vadd(u, w);
+            a[blk + i + H] = mul_w32<T, i * (32 / (2 * H))>(vsub(u, w));
+          });
+        });
+      }
+    });
+    V t[R];
+    static_for<0, R>([&](auto kIC) {
+      constexpr int k = decltype(kIC)::value;
+      t[k] = a[bitrev<R>(k)];
+    });
+    static_for<0, R>([&](auto kIC) {
+      constexpr int k = decltype(kIC)::value;
+      a[k] = t[k];
+    });
+  }
+}
+
+// Multiply a[1..R-1] by W^r given W = w1, using binary splitting.
+template <int R, typename V>
+__device__ __forceinline__ void apply_twiddles(V *a, V w1) {
+  if constexpr (R > 1) {
+    V w[R];
+    w[1] = w1;
+    static_for<2, R>([&](auto rIC) {
+      constexpr int r = decltype(rIC)::value;
+      w[r] = vmul(w[r / 2], w[r - r / 2]);
+    });
+    static_for<1, R>([&](auto rIC) {
+      constexpr int r = decltype(rIC)::value;
+      a[r] = vmul(a[r], w[r]);
+    });
+  }
+}
+
+// Padded shared-memory index: one spare slot every 16 values.
+__device__ __forceinline__ int spad(int i) { return i + (i >> 4); }
+__host__ __device__ constexpr int spad_size(int L) { return L + (L >> 4); }
+
+// Compile-time pass plan: radix of pass p and the product of earlier radices.
+template <int L, int E> struct Plan {
+  __host__ __device__ static constexpr int radix(int p) {
+    int ns = 1;
+    for (int i = 0; i < p; ++i) {
+      int r = (L / ns) < E ? (L / ns) : E;
+      ns *= r;
+    }
+    return (L / ns) < E ? (L / ns) : E;
+  }
+  __host__ __device__ static constexpr int ns(int p) {
+    int ns = 1;
+    for (int i = 0; i < p; ++i)
+      ns *= radix(i);
+    return ns;
+  }
+  __host__ __device__ static constexpr int passes() {
+    int n = 0, ns = 1;
+    while (ns < L) {
+      ns *= radix(n);
+      ++n;
+    }
+    return n;
+  }
+};
+
+// Group barrier: the P threads of group g (named barrier g+1), or the whole
+// CTA when the CTA holds a single group.
+template <int G, int P> __device__ __forceinline__ void group_sync(int g) {
+  if constexpr (G == 1) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"r"(g + 1), "r"(P) : "memory");
+  }
+}
+
+// One Stockham pass reading `v` (registers: butterfly b, element r at
+// v[b*R + r]) that were loaded for this pass, applying twiddles and the
+// R-point DFTs in place.  Index bookkeeping for the surrounding exchange is
+// done by the callers.
+template <typename T, int L, int E, int P, int PASS, typename V>
+__device__ __forceinline__ void pass_compute(V *v, int t, const V *tw) {
+  using PL = Plan<L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int NS = PL::ns(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    if constexpr (NS > 1) {
+      const int j = t + b * P;
+      const int k = j & (NS - 1);
+      // W_{NS*R}^k = W_L^{k * L/(NS*R)}
+      const V w1 = tw[k * (L / (NS * R))];
+      apply_twiddles<R>(v + b * R, w1);
+    }
+    dft_reg<T, R>(v + b * R);
+  });
+}
+
+// Write the outputs of pass PASS to shared memory.
+template <int L, int E, int P, int PASS, typename V>
+__device__ __forceinline__ void pass_store(const V *v, V *buf, int t) {
+  using PL = Plan<L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int NS = PL::ns(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    const int j = t + b * P;
+    const int k = j & (NS - 1);
+    const int base = (j / NS) * NS * R + k;
+    static_for<0, R>([&](auto rIC) {
+      constexpr int r = decltype(rIC)::value;
+      buf[spad(base + r * NS)] = v[b * R + r];
+    });
+  });
+}
+
+// Read the inputs of pass PASS from shared memory.
+template <int L, int E, int P, int PASS, typename V>
+__device__ __forceinline__ void pass_load(V *v, const V *buf, int t) {
+  using PL = Plan<L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    const int j = t + b * P;
+    static_for<0, R>([&](auto rIC) {
+      constexpr int r = decltype(rIC)::value;
+      v[b * R + r] = buf[spad(j + r * (L / R))];
+    });
+  });
+}
+
+// Full transform after pass 0's inputs are in registers.  On return v holds
+// the DFT: v[b*R + r] = X[t + b*P + r*(L/R)] with R the last radix.
+// buf is the group's padded buffer (spad_size(L) values).
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group(V *v, V *buf, int t, int g,
+                                          const V *tw) {
+  constexpr int NP = Plan<L, E>::passes();
+  static_for<0, NP>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g); // every read of this pass done before rewriting
+    }
+    pass_compute<T, L, E, P, p>(v, t, tw);
+    if constexpr (p + 1 < NP) {
+      pass_store<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+  });
+}
+
+// Position (natural-order bin) of register slot e after fft_group.
+template <int L, int E, int P>
+__device__ __forceinline__ int out_bin(int t, int e) {
+  constexpr int R = Plan<L, E>::radix(Plan<L, E>::passes() - 1);
+  return t + (e / R) * P + (e % R) * (L / R);
+}
+
+// Position (time index) of register slot e for pass-0 inputs.
+template <int L, int E, int P>
+__device__ __forceinline__ int in_index(int t, int e) {
+  constexpr int R = Plan<L, E>::radix(0);
+  return t + (e / R) * P + (e % R) * (L / R);
+}
+
+} // namespace ib200

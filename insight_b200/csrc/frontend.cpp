@@ -1,0 +1,631 @@
+// frontend.cpp — host side of the B200 spectral backend.
+//
+// Mirrors the reference frontend ins::signal::{csd, welch, spectrogram, stft}
+// (src/ops/signal/spectral_analysis.cpp:104-334): argument defaults, framing,
+// window and scale, result arrays and error messages.  Instead of the
+// reference's per-segment composite loop (~25 registry ops per segment) it
+// plans one launch of the fused kernel family (spectral_kernels.cuh) over
+// every segment of every channel.
+//
+// Differences from the reference, all deliberate:
+//  * F32 welch/csd/spectrogram('psd') work (the reference throws in
+//    compute_psd_scale, :63, because it calls item<double>() on an F32 sum);
+//    the scale is computed in F64 from the F32-rounded window.
+//  * 2-D inputs are a batch of channels (the reference accepts 1-D only).
+//  * nfft must be a power of two in [16, 8192] and >= nperseg; noverlap must
+//    be < nperseg (the reference divides by a non-positive step otherwise).
+#include "frontend.h"
+#include "launch.h"
+#include "windows.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <vector>
+
+#ifndef M_PI
+#define M_PI 3.14159265358979323846
+#endif
+
+namespace ib200 {
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic<int64_t> g_launches{0};
+} // namespace
+
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+const char *last_error() { return g_last_error.c_str(); }
+int64_t launch_count() { return g_launches.load(); }
+
+struct Fail : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+static void check(bool ok, const std::string &msg) {
+  if (!ok)
+    throw Fail(msg);
+}
+
+static void cuda_check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    std::ostringstream o;
+    o << what << ": " << cudaGetErrorString(e);
+    throw Fail(o.str());
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-device state: stream, grow-only buffers, constant tables.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t n = 0;
+};
+
+struct DeviceState {
+  int dev = 0;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  DevBuf scratch, xin, yin, out, win_tmp;
+  std::map<std::string, DevBuf> tables;
+};
+
+std::mutex g_states_mu;
+std::map<int, std::unique_ptr<DeviceState>> g_states;
+
+DeviceState &device_state(int dev) {
+  std::lock_guard<std::mutex> lk(g_states_mu);
+  auto &slot = g_states[dev];
+  if (!slot) {
+    auto st = std::make_unique<DeviceState>();
+    st->dev = dev;
+    cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    cuda_check(cudaDeviceGetAttribute(&st->num_sms,
+                                      cudaDevAttrMultiProcessorCount, dev),
+               "cudaDeviceGetAttribute");
+    int major = 0;
+    cuda_check(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor,
+                                      dev),
+               "cudaDeviceGetAttribute");
+    check(major == 10, "insight_b200: device " + std::to_string(dev) +
+                           " is not an sm_100 (B200) GPU");
+    cuda_check(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking),
+               "cudaStreamCreate");
+    slot = std::move(st);
+  }
+  return *slot;
+}
+
+void ensure(DevBuf &b, size_t bytes) {
+  if (b.n >= bytes && b.p)
+    return;
+  if (b.p) {
+    cuda_check(cudaFree(b.p), "cudaFree");
+    b.p = nullptr;
+    b.n = 0;
+  }
+  size_t n = std::max<size_t>(bytes, 256);
+  cuda_check(cudaMalloc(&b.p, n), "cudaMalloc");
+  b.n = n;
+}
+
+size_t dtype_size(int32_t dt) {
+  switch (dt) {
+  case INSIGHT_DTYPE_F32: return 4;
+  case INSIGHT_DTYPE_F64: return 8;
+  case INSIGHT_DTYPE_C32: return 8;
+  case INSIGHT_DTYPE_C64: return 16;
+  default: return 0;
+  }
+}
+
+template <typename T>
+std::vector<unsigned char> pack_complex(const std::vector<double> &re,
+                                        const std::vector<double> &im) {
+  std::vector<unsigned char> b(re.size() * 2 * sizeof(T));
+  T *p = reinterpret_cast<T *>(b.data());
+  for (size_t i = 0; i < re.size(); ++i) {
+    p[2 * i] = (T)re[i];
+    p[2 * i + 1] = (T)im[i];
+  }
+  return b;
+}
+
+const void *table(DeviceState &st, const std::string &key,
+                  const std::vector<unsigned char> &bytes) {
+  auto it = st.tables.find(key);
+  if (it != st.tables.end())
+    return it->second.p;
+  DevBuf b;
+  ensure(b, bytes.size());
+  cuda_check(cudaMemcpy(b.p, bytes.data(), bytes.size(), cudaMemcpyHostToDevice),
+             "cudaMemcpy");
+  st.tables[key] = b;
+  return b.p;
+}
+
+// W_L^m = exp(-2 pi i m / L), evaluated in double.
+const void *twiddles(DeviceState &st, int64_t L, bool f64) {
+  std::vector<double> re(L), im(L);
+  for (int64_t m = 0; m < L; ++m) {
+    const double a = 2.0 * M_PI * (double)m / (double)L;
+    re[m] = std::cos(a);
+    im[m] = -std::sin(a);
+  }
+  std::string key = std::string("tw|") + (f64 ? "d|" : "f|") + std::to_string(L);
+  return table(st, key, f64 ? pack_complex<double>(re, im)
+                            : pack_complex<float>(re, im));
+}
+
+// D[k] = sum_{n < M} W_L^{nk} = (1 - W^{kM}) / (1 - W^k), D[0] = M.
+const void *dc_table(DeviceState &st, int64_t L, int64_t M, bool f64) {
+  std::vector<double> re(L), im(L);
+  for (int64_t k = 0; k < L; ++k) {
+    if (k == 0) {
+      re[k] = (double)M;
+      im[k] = 0.0;
+      continue;
+    }
+    const double a1 = -2.0 * M_PI * (double)k / (double)L;
+    const double aM = -2.0 * M_PI * (double)((k * M) % L) / (double)L;
+    const double nr = 1.0 - std::cos(aM), ni = -std::sin(aM);
+    const double dr = 1.0 - std::cos(a1), di = -std::sin(a1);
+    const double den = dr * dr + di * di;
+    re[k] = (nr * dr + ni * di) / den;
+    im[k] = (ni * dr - nr * di) / den;
+  }
+  std::string key = std::string("dc|") + (f64 ? "d|" : "f|") +
+                    std::to_string(L) + "|" + std::to_string(M);
+  return table(st, key, f64 ? pack_complex<double>(re, im)
+                            : pack_complex<float>(re, im));
+}
+
+// Window values cast to the compute dtype and zero padded to nfft.
+std::vector<unsigned char> window_bytes(const std::vector<double> &w,
+                                        int64_t nfft, bool f64) {
+  std::vector<unsigned char> b(nfft * (f64 ? 8 : 4), 0);
+  for (size_t i = 0; i < w.size(); ++i) {
+    if (f64)
+      reinterpret_cast<double *>(b.data())[i] = w[i];
+    else
+      reinterpret_cast<float *>(b.data())[i] = (float)w[i];
+  }
+  return b;
+}
+
+// compute_psd_scale (spectral_analysis.cpp:57-67) on the window as the
+// kernel sees it (rounded to the compute dtype), summed in F64.
+double window_sum_sq(const std::vector<double> &w, bool f64) {
+  double s = 0.0;
+  for (double v : w) {
+    const double r = f64 ? v : (double)(float)v;
+    s += r * r;
+  }
+  return s;
+}
+
+// Element view of one input: channel c, sample n at base + c*cs + n*ss.
+struct InView {
+  const InsightArray *a = nullptr;
+  int64_t C = 1, N = 0, cs = 0, ss = 1;
+  bool gpu = false;
+  int dev = 0;
+  int32_t dtype = 0;
+  int64_t span = 0; // elements from the first addressed element to the last
+};
+
+InView view_input(const InsightArray *a, int axis, const char *op) {
+  InView v;
+  check(a != nullptr && a->ndim >= 1,
+        std::string(op) + ": inputs are undefined");
+  check(a->dtype == INSIGHT_DTYPE_F32 || a->dtype == INSIGHT_DTYPE_F64,
+        std::string(op) + ": input dtype must be F32 or F64 on the B200 backend");
+  check(a->ndim <= 2, std::string(op) +
+                          ": inputs must be 1-D or 2-D (channels x samples)");
+  v.a = a;
+  v.dtype = a->dtype;
+  v.gpu = a->device_type == INSIGHT_DEVICE_GPU;
+  v.dev = a->device_id;
+  if (a->ndim == 1) {
+    v.N = a->dims[0];
+    v.ss = a->strides[0];
+  } else {
+    int ax = axis < 0 ? axis + 2 : axis;
+    check(ax == 0 || ax == 1, std::string(op) + ": axis out of range");
+    v.N = a->dims[ax];
+    v.ss = a->strides[ax];
+    v.C = a->dims[1 - ax];
+    v.cs = a->strides[1 - ax];
+  }
+  check(v.ss > 0 && v.cs >= 0,
+        std::string(op) + ": negative or zero sample strides are not supported");
+  v.span = (v.N > 0 ? (v.N - 1) * v.ss : 0) + (v.C > 0 ? (v.C - 1) * v.cs : 0) + 1;
+  return v;
+}
+
+const char *base_ptr(const InsightArray *a) {
+  return reinterpret_cast<const char *>(a->data) +
+         a->offset * (int64_t)dtype_size(a->dtype);
+}
+
+int64_t numel(const InsightArray *a) {
+  int64_t n = 1;
+  for (int i = 0; i < a->ndim; ++i)
+    n *= a->dims[i];
+  return n;
+}
+
+bool contiguous(const InsightArray *a) {
+  int64_t s = 1;
+  for (int i = a->ndim - 1; i >= 0; --i) {
+    if (a->dims[i] != 1 && a->strides[i] != s)
+      return false;
+    s *= a->dims[i];
+  }
+  return true;
+}
+
+// Write host F64 values into a caller array (CPU or GPU, contiguous F64).
+void put_host_vector(const std::vector<double> &v, InsightArray *dst,
+                     const char *what, cudaStream_t stream) {
+  if (!dst)
+    return;
+  check(dst->dtype == INSIGHT_DTYPE_F64,
+        std::string(what) + " must be an F64 array");
+  check(numel(dst) == (int64_t)v.size(),
+        std::string(what) + " has " + std::to_string(numel(dst)) +
+            " elements, expected " + std::to_string(v.size()));
+  check(contiguous(dst), std::string(what) + " must be contiguous");
+  char *p = reinterpret_cast<char *>(dst->data) + dst->offset * 8;
+  if (dst->device_type == INSIGHT_DEVICE_GPU) {
+    cuda_check(cudaMemcpyAsync(p, v.data(), v.size() * 8, cudaMemcpyHostToDevice,
+                               stream),
+               "cudaMemcpyAsync");
+    cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+  } else {
+    std::memcpy(p, v.data(), v.size() * 8);
+  }
+}
+
+} // namespace
+
+// ---------------------------------------------------------------------------
+// One spectral call.
+// ---------------------------------------------------------------------------
+C_Status run(const Call &c) {
+  try {
+    // welch runs csd(x, x) in the reference (spectral_analysis.cpp:177-183)
+    // and stft runs spectrogram (:330-334), so their messages carry those names.
+    const char *op = (c.op == INSIGHT_B200_OP_CSD || c.op == INSIGHT_B200_OP_WELCH)
+                         ? "csd"
+                         : "spectrogram";
+    const bool acc = (c.op == INSIGHT_B200_OP_WELCH || c.op == INSIGHT_B200_OP_CSD);
+    check(c.nperseg > 0, std::string(op) + ": nperseg must be positive");
+    InView xv = view_input(c.x, c.axis, op);
+    InView yv = xv;
+    if (c.op == INSIGHT_B200_OP_CSD) {
+      check(c.y != nullptr, "csd: inputs are undefined");
+      yv = view_input(c.y, c.axis, op);
+      check(yv.dtype == xv.dtype, "csd: x and y must have the same dtype");
+      check(yv.N == xv.N && yv.C == xv.C,
+            "csd: x and y must have the same shape");
+      check(yv.gpu == xv.gpu && (!xv.gpu || yv.dev == xv.dev),
+            "csd: x and y must be on the same device");
+    }
+    const bool f64 = xv.dtype == INSIGHT_DTYPE_F64;
+
+    // Defaults (spectral_analysis.cpp:114-117 and :235-238).
+    int64_t nfft = c.nfft == 0 ? c.nperseg : c.nfft;
+    int64_t noverlap = c.noverlap;
+    if (noverlap == 0)
+      noverlap = acc ? c.nperseg / 2 : c.nperseg / 8;
+    const int64_t step = c.nperseg - noverlap;
+    check(step > 0, std::string(op) + ": noverlap must be less than nperseg");
+    const int64_t N = xv.N;
+    const int64_t S = (N >= c.nperseg) ? ((N - c.nperseg) / step + 1) : 0;
+    check(S >= 1, acc ? std::string(op) + ": signal too short for given nperseg"
+                      : std::string("spectrogram: signal too short"));
+    check(nfft_supported(nfft),
+          std::string(op) + ": nfft must be a power of two in [16, 8192] on the "
+                            "B200 backend (got " + std::to_string(nfft) + ")");
+    check(nfft >= c.nperseg,
+          std::string(op) + ": nfft must be >= nperseg on the B200 backend");
+    const bool onesided = c.onesided;
+    const int64_t F = onesided ? nfft / 2 + 1 : nfft;
+
+    int64_t seg0 = c.seg_begin, seg1 = c.seg_end <= 0 ? S : c.seg_end;
+    check(seg0 >= 0 && seg0 < seg1 && seg1 <= S,
+          std::string(op) + ": segment range out of bounds");
+
+    // Window: caller values (registry kernels) or by name.
+    std::vector<double> w;
+    if (c.window_values) {
+      w = *c.window_values;
+      check((int64_t)w.size() == c.nperseg,
+            std::string(op) + ": window must have nperseg values");
+    } else {
+      try {
+        w = get_window(c.window, c.nperseg, false);
+      } catch (const std::invalid_argument &e) {
+        throw Fail(e.what());
+      }
+    }
+    double scale = c.has_scale ? c.scale
+                               : ((c.scaling == "density" ? c.fs : 1.0) /
+                                  window_sum_sq(w, f64));
+    const int dc_mode = !c.detrend_constant ? 0 : (nfft == c.nperseg ? 1 : 2);
+
+    // Result geometry and output arrays.
+    std::vector<double> fvec(F);
+    const double df = c.fs / (double)nfft;
+    for (int64_t i = 0; i < F; ++i)
+      fvec[i] = i * df;
+    std::vector<double> tvec(S);
+    for (int64_t i = 0; i < S; ++i)
+      tvec[i] = (i * step + c.nperseg / 2.0) / c.fs;
+
+    const int dev = xv.gpu ? xv.dev : c.default_device;
+    cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    DeviceState &st = device_state(dev);
+    std::lock_guard<std::mutex> lk(st.mu);
+    cudaStream_t stream = c.stream ? c.stream : st.stream;
+
+    LaunchDesc d;
+    d.f64 = f64;
+    d.nfft = nfft;
+    d.nperseg = c.nperseg;
+    d.step = step;
+    d.C = xv.C;
+    d.seg0 = seg0;
+    d.S = seg1 - seg0;
+    d.x_cs = xv.cs;
+    d.x_ss = xv.ss;
+    d.y_cs = yv.cs;
+    d.y_ss = yv.ss;
+    d.F = F;
+    d.onesided_mask = onesided && nfft > 1;
+    d.dc_mode = dc_mode;
+
+    // Inputs: GPU arrays in place, CPU arrays copied over their span.
+    auto stage = [&](const InView &v, DevBuf &buf) -> const void * {
+      const size_t es = dtype_size(v.dtype);
+      if (v.gpu) {
+        check(v.dev == dev, std::string(op) + ": inputs on different devices");
+        return base_ptr(v.a);
+      }
+      ensure(buf, v.span * es);
+      cuda_check(cudaMemcpyAsync(buf.p, base_ptr(v.a), v.span * es,
+                                 cudaMemcpyHostToDevice, stream),
+                 "cudaMemcpyAsync");
+      return buf.p;
+    };
+    d.x = stage(xv, st.xin);
+    d.y = (c.op == INSIGHT_B200_OP_CSD) ? stage(yv, st.yin) : nullptr;
+
+    // Tables.
+    if (c.window_values) {
+      auto wb = window_bytes(w, nfft, f64);
+      ensure(st.win_tmp, wb.size());
+      cuda_check(cudaMemcpyAsync(st.win_tmp.p, wb.data(), wb.size(),
+                                 cudaMemcpyHostToDevice, stream),
+                 "cudaMemcpyAsync");
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+      d.win = st.win_tmp.p;
+    } else {
+      std::string key = std::string("win|") + (f64 ? "d|" : "f|") + c.window +
+                        "|" + std::to_string(c.nperseg) + "|" +
+                        std::to_string(nfft);
+      d.win = table(st, key, window_bytes(w, nfft, f64));
+    }
+    d.tw = twiddles(st, nfft, f64);
+    d.dtab = dc_mode == 2 ? dc_table(st, nfft, c.nperseg, f64) : nullptr;
+
+    // Output array.
+    InsightArray *out = c.out;
+    check(out != nullptr, std::string(op) + ": output array is undefined");
+    const bool out_complex =
+        out->dtype == INSIGHT_DTYPE_C32 || out->dtype == INSIGHT_DTYPE_C64;
+    check(out->dtype == INSIGHT_DTYPE_F64 || out_complex,
+          std::string(op) + ": output must be F64, C32 or C64");
+    const size_t oes = dtype_size(out->dtype);
+    const bool out_gpu = out->device_type == INSIGHT_DEVICE_GPU;
+    check(!out_gpu || out->device_id == dev,
+          std::string(op) + ": output on a different device");
+    const int64_t Sl = seg1 - seg0;
+    int64_t o_cs = 0, o_rs = 0, o_ts = 0;
+    int64_t out_elems = 0;
+    if (acc) {
+      // [F] or [C, F]
+      out_elems = xv.C * F;
+      check(numel(out) == out_elems,
+            std::string(op) + ": output must have " + std::to_string(out_elems) +
+                " elements");
+      check(out->dims[out->ndim - 1] == F && out->strides[out->ndim - 1] == 1,
+            std::string(op) + ": output bins must be the last, unit-stride axis");
+      o_cs = out->ndim >= 2 ? out->strides[out->ndim - 2] : F;
+      if (c.op == INSIGHT_B200_OP_WELCH) {
+        d.kind = LK_PSD;
+        check(out->dtype == INSIGHT_DTYPE_F64, "welch: output must be F64");
+        d.out_kind = c.raw_sums ? OUT_RAW_F64_K : OUT_REAL_F64_K;
+      } else {
+        d.kind = LK_CSD;
+        if (c.raw_sums) {
+          check(out->dtype == INSIGHT_DTYPE_C64,
+                "csd: raw sums need a C64 (complex128) output");
+          d.out_kind = OUT_RAW_F64_K;
+        } else if (out->dtype == INSIGHT_DTYPE_F64) {
+          d.out_kind = OUT_REAL_F64_K;
+        } else {
+          d.out_kind = out->dtype == INSIGHT_DTYPE_C32 ? OUT_C64_K : OUT_C128_K;
+        }
+      }
+      d.avg_scale = scale / (double)S;
+    } else {
+      d.kind = LK_STORE;
+      // complex: [C?, F, Sl]; F64: [C?, Sl, F] (the reference's transposed view)
+      out_elems = xv.C * F * Sl;
+      check(numel(out) == out_elems,
+            std::string(op) + ": output must have " + std::to_string(out_elems) +
+                " elements");
+      const int nd = out->ndim;
+      check(nd >= 2 && (nd == 2 ? xv.C == 1 : nd == 3),
+            std::string(op) + ": output must be 2-D (or 3-D for a batch)");
+      if (out_complex) {
+        o_rs = out->strides[nd - 2];
+        o_ts = out->strides[nd - 1];
+        check(out->dims[nd - 2] == F && out->dims[nd - 1] == Sl,
+              std::string(op) + ": complex output must be (n_freq, n_seg)");
+      } else {
+        o_ts = out->strides[nd - 2];
+        o_rs = out->strides[nd - 1];
+        check(out->dims[nd - 2] == Sl && out->dims[nd - 1] == F,
+              std::string(op) + ": F64 output must be (n_seg, n_freq)");
+      }
+      o_cs = nd == 3 ? out->strides[0] : 0;
+      if (out_complex) {
+        const bool want = f64 ? out->dtype == INSIGHT_DTYPE_C64
+                              : out->dtype == INSIGHT_DTYPE_C32;
+        check(want, std::string(op) +
+                        ": complex output must be C32 for F32 input, C64 for F64");
+        d.out_kind = f64 ? OUT_C128_K : OUT_C64_K;
+      } else if (c.mode == "psd") {
+        d.out_kind = OUT_PSD_F64_K;
+      } else if (c.mode == "complex") {
+        d.out_kind = OUT_REAL_F64_K;
+      } else {
+        d.out_kind = OUT_MAG_F64_K;
+      }
+      d.psd_scale = scale; // spectrogram psd uses 'density' scaling (:304)
+    }
+
+    // Where the kernel writes: the caller's GPU array, or a device buffer
+    // that is copied back to the caller's CPU array.
+    bool direct = out_gpu;
+    int64_t span = 0;
+    {
+      int64_t lo = 0, hi = 0;
+      for (int i = 0; i < out->ndim; ++i) {
+        check(out->strides[i] >= 0, std::string(op) + ": negative output strides");
+        hi += (out->dims[i] - 1) * out->strides[i];
+      }
+      span = hi - lo + 1;
+    }
+    void *obase;
+    if (direct) {
+      obase = reinterpret_cast<char *>(out->data) + out->offset * (int64_t)oes;
+    } else {
+      ensure(st.out, span * oes);
+      obase = st.out.p;
+    }
+    d.out = obase;
+    d.o_cs = o_cs;
+    d.o_rs = o_rs;
+    d.o_ts = o_ts;
+
+    // Scratch and launch.
+    const size_t sb = scratch_bytes(d, st.num_sms);
+    if (sb)
+      ensure(st.scratch, sb);
+    int64_t nl = 0;
+    cuda_check(launch(d, st.scratch.p, st.num_sms, stream, &nl), "kernel launch");
+    g_launches += nl;
+
+    if (!direct) {
+      char *hp = reinterpret_cast<char *>(out->data) + out->offset * (int64_t)oes;
+      cuda_check(cudaMemcpyAsync(hp, obase, span * oes, cudaMemcpyDeviceToHost,
+                                 stream),
+                 "cudaMemcpyAsync");
+    }
+    const bool must_sync = c.sync || !xv.gpu || !direct ||
+                           (c.op == INSIGHT_B200_OP_CSD && !yv.gpu);
+    if (must_sync)
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    else
+      cuda_check(cudaGetLastError(), "kernel launch");
+
+    put_host_vector(fvec, c.f, "f", stream);
+    put_host_vector(tvec, c.t, "t", stream);
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+C_Status shape(const Call &c, int64_t *n_channels, int64_t *n_seg,
+               int64_t *n_freq) {
+  try {
+    const bool acc = (c.op == INSIGHT_B200_OP_WELCH || c.op == INSIGHT_B200_OP_CSD);
+    const char *op = acc ? "csd" : "spectrogram";
+    check(c.nperseg > 0, std::string(op) + ": nperseg must be positive");
+    InView xv = view_input(c.x, c.axis, op);
+    int64_t nfft = c.nfft == 0 ? c.nperseg : c.nfft;
+    int64_t noverlap = c.noverlap == 0 ? (acc ? c.nperseg / 2 : c.nperseg / 8)
+                                       : c.noverlap;
+    const int64_t step = c.nperseg - noverlap;
+    check(step > 0, std::string(op) + ": noverlap must be less than nperseg");
+    const int64_t N = xv.N;
+    const int64_t S = (N >= c.nperseg) ? ((N - c.nperseg) / step + 1) : 0;
+    if (n_channels)
+      *n_channels = xv.C;
+    if (n_seg)
+      *n_seg = S;
+    if (n_freq)
+      *n_freq = c.onesided ? nfft / 2 + 1 : nfft;
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+// Scale and mask reduced raw sums in place (after a cross-device reduction).
+C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums) {
+  try {
+    check(sums && sums->device_type == INSIGHT_DEVICE_GPU,
+          "finalize_sums: sums must be a GPU array");
+    const bool f64 = c.x_dtype == INSIGHT_DTYPE_F64;
+    std::vector<double> w;
+    try {
+      w = get_window(c.window, c.nperseg, false);
+    } catch (const std::invalid_argument &e) {
+      throw Fail(e.what());
+    }
+    const double scale =
+        (c.scaling == "density" ? c.fs : 1.0) / window_sum_sq(w, f64);
+    const int64_t nfft = c.nfft == 0 ? c.nperseg : c.nfft;
+    const int64_t F = c.onesided ? nfft / 2 + 1 : nfft;
+    const bool cplx = sums->dtype == INSIGHT_DTYPE_C64;
+    check(sums->dtype == INSIGHT_DTYPE_F64 || cplx,
+          "finalize_sums: sums must be F64 or C64");
+    check(contiguous(sums) && numel(sums) % F == 0,
+          "finalize_sums: sums must be a contiguous [C, n_freq] array");
+    const int64_t C = numel(sums) / F;
+    cuda_check(cudaSetDevice(sums->device_id), "cudaSetDevice");
+    DeviceState &st = device_state(sums->device_id);
+    std::lock_guard<std::mutex> lk(st.mu);
+    cudaStream_t stream = c.stream ? c.stream : st.stream;
+    double *p = reinterpret_cast<double *>(sums->data) +
+                sums->offset * (cplx ? 2 : 1);
+    cuda_check(scale_sums(p, C, F, cplx, scale / (double)S_total,
+                          c.onesided && nfft > 1, stream),
+               "finalize_sums");
+    g_launches += 1;
+    if (c.sync)
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+} // namespace ib200

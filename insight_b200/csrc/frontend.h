@@ -1,0 +1,49 @@
+// frontend.h — host planner of the B200 spectral backend (C++ side of the
+// C ABI in include/insight_b200.h).
+#pragma once
+#include "insight_b200.h"
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace ib200 {
+
+// One spectral call, with the reference frontend's arguments.
+struct Call {
+  int op = INSIGHT_B200_OP_WELCH;
+  const InsightArray *x = nullptr;
+  const InsightArray *y = nullptr;
+  InsightArray *out = nullptr; // Pxx / Pxy / Sxx / Zxx
+  InsightArray *f = nullptr;   // optional
+  InsightArray *t = nullptr;   // optional
+  int axis = -1;
+  double fs = 1.0;
+  std::string window = "hann";
+  const std::vector<double> *window_values = nullptr; // registry kernels
+  int64_t nperseg = 256, noverlap = 0, nfft = 0;
+  bool detrend_constant = true;
+  bool onesided = true;
+  std::string scaling = "density";
+  std::string mode = "psd";
+  bool has_scale = false; // registry kernels pass the frontend's scale
+  double scale = 1.0;
+  int64_t seg_begin = 0, seg_end = 0;
+  bool raw_sums = false;
+  int32_t x_dtype = 0;    // finalize_sums only
+  int default_device = 0; // device for CPU inputs
+  cudaStream_t stream = nullptr;
+  bool sync = true;
+};
+
+C_Status run(const Call &c);
+C_Status shape(const Call &c, int64_t *n_channels, int64_t *n_seg,
+               int64_t *n_freq);
+C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums);
+
+void set_last_error(const std::string &msg);
+const char *last_error();
+int64_t launch_count();
+
+} // namespace ib200

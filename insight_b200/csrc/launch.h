@@ -1,0 +1,73 @@
+// launch.h — device-side launch interface shared by the frontend and the
+// per-dtype kernel translation units.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ib200 {
+
+enum LaunchKind { LK_PSD = 0, LK_CSD = 1, LK_STORE = 2 };
+
+// What the kernels write.
+enum OutKindK {
+  OUT_C64_K = 0,      // complex64 (store kernel: complex of the compute dtype)
+  OUT_REAL_F64_K = 1, // Re(.) as double: reference csd/welch value, stft
+  OUT_PSD_F64_K = 2,  // |X|^2 * scale * mask as double (spectrogram 'psd')
+  OUT_MAG_F64_K = 3,  // |X| as double (spectrogram 'magnitude')
+  OUT_RAW_F64_K = 4,  // unscaled sums (welch: double, csd: double2)
+  OUT_C128_K = 5,     // complex128
+};
+
+struct LaunchDesc {
+  int kind = LK_PSD;
+  bool f64 = false;       // compute dtype: false f32, true f64
+  int64_t nfft = 0;       // transform length L (power of two, 16..8192)
+  int64_t nperseg = 0, step = 0;
+  int64_t C = 1;          // channels
+  int64_t seg0 = 0;       // first segment handled by this launch
+  int64_t S = 0;          // segments handled by this launch, per channel
+  const void *x = nullptr, *y = nullptr; // sample 0 of channel 0
+  int64_t x_cs = 0, x_ss = 1, y_cs = 0, y_ss = 1;
+  const void *win = nullptr;  // [nfft] window in compute dtype
+  const void *tw = nullptr;   // [nfft] twiddles in compute dtype
+  const void *dtab = nullptr; // [nfft] detrend correction table
+  int dc_mode = 0;
+  int64_t F = 0;              // bins written
+  bool onesided_mask = false;
+  // welch / csd result
+  double avg_scale = 1.0;
+  int out_kind = 0;           // OutKindK
+  void *out = nullptr;
+  int64_t o_cs = 0, o_rs = 0, o_ts = 0; // elements
+  double psd_scale = 1.0;     // spectrogram 'psd'
+};
+
+// Bytes of scratch the launch needs (welch / csd unit partials).
+size_t scratch_bytes(const LaunchDesc &d, int num_sms);
+
+// Enqueue the kernels on `stream`.  scratch must hold scratch_bytes(d).
+cudaError_t launch(const LaunchDesc &d, void *scratch, int num_sms,
+                   cudaStream_t stream, int64_t *launches);
+
+bool nfft_supported(int64_t nfft);
+
+// Per-dtype entry points (one translation unit each).
+cudaError_t launch_f32(const LaunchDesc &d, void *scratch, int num_sms,
+                       cudaStream_t stream, int64_t *launches);
+cudaError_t launch_f64(const LaunchDesc &d, void *scratch, int num_sms,
+                       cudaStream_t stream, int64_t *launches);
+
+// Work split of the welch / csd kernels.
+struct AccSplit {
+  int64_t Tc, Qt, nq, U;
+  int grid;
+};
+AccSplit acc_split(const LaunchDesc &d, int num_sms, int blocks_per_sm);
+
+// sums[c, k] *= factor * (mask && 1 <= k <= F-2 ? 2 : 1); complex sums are
+// interleaved double pairs.
+cudaError_t scale_sums(double *sums, int64_t C, int64_t F, bool complex_sums,
+                       double factor, bool mask, cudaStream_t stream);
+
+} // namespace ib200

@@ -1,0 +1,110 @@
+"""ctypes wrapper of the reference built from its sources (oracle/_ref).
+
+Test infrastructure only: runs the reference's own ins::signal::welch / csd /
+spectrogram / stft (src/ops/signal/spectral_analysis.cpp) through
+oracle/ref_harness.cpp.  The reference's CPU "fft" kernel exists only with
+FFTW3, which is absent here; the harness registers a substitute DFT kernel
+through the reference's insight_register_kernel C ABI (see ref_harness.cpp).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from .spectral_oracle import framing
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "_ref")
+HARNESS = os.path.join(REF_DIR, "libinsight_ref_harness.so")
+
+_lib = None
+
+
+def available() -> bool:
+    return os.path.exists(HARNESS) and os.path.exists(
+        os.path.join(REF_DIR, "libinsight_cpu_backend.so"))
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not available():
+            raise RuntimeError("oracle/_ref is not built (make -C oracle ref)")
+        L = ctypes.CDLL(HARNESS, mode=ctypes.RTLD_GLOBAL)
+        L.ref_last_error.restype = ctypes.c_char_p
+        L.ref_init.argtypes = [ctypes.c_char_p]
+        P = ctypes.POINTER(ctypes.c_double)
+        I = ctypes.c_int64
+        L.ref_csd.argtypes = [ctypes.c_void_p, ctypes.c_void_p, I, ctypes.c_int,
+                              ctypes.c_double, ctypes.c_char_p, I, I, I,
+                              ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p, P, P, I,
+                              ctypes.POINTER(I)]
+        L.ref_spectrogram.argtypes = [ctypes.c_void_p, I, ctypes.c_int, ctypes.c_double,
+                                      ctypes.c_char_p, I, I, I, ctypes.c_char_p,
+                                      ctypes.c_int, ctypes.c_char_p, ctypes.c_int, P, P,
+                                      P, I, ctypes.POINTER(I), ctypes.POINTER(I)]
+        if L.ref_init(REF_DIR.encode()) != 0:
+            raise RuntimeError("ref_init: " + L.ref_last_error().decode())
+        _lib = L
+    return _lib
+
+
+def _dt(x):
+    return 9 if x.dtype == np.float32 else 10
+
+
+def csd(x, y=None, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
+        detrend="constant", return_onesided=True, scaling="density"):
+    """Reference csd (y given) or welch (y None): returns (f, Pxx) F64."""
+    L = lib()
+    x = np.ascontiguousarray(x)
+    if y is not None:
+        y = np.ascontiguousarray(y, dtype=x.dtype)
+    cap = (nfft or nperseg) + 2
+    f = np.zeros(cap)
+    p = np.zeros(cap)
+    nf = ctypes.c_int64()
+    P = ctypes.POINTER(ctypes.c_double)
+    rc = L.ref_csd(x.ctypes.data, None if y is None else y.ctypes.data, len(x), _dt(x),
+                   fs, window.encode(), nperseg, noverlap, nfft, detrend.encode(),
+                   1 if return_onesided else 0, scaling.encode(),
+                   f.ctypes.data_as(P), p.ctypes.data_as(P), cap, ctypes.byref(nf))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    return f[:nf.value].copy(), p[:nf.value].copy()
+
+
+def welch(x, **kw):
+    return csd(x, None, **kw)
+
+
+def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
+                detrend="constant", return_onesided=True, mode="psd", is_stft=False):
+    """Reference spectrogram / stft: returns (f, t, Sxx) with Sxx (n_seg, n_freq)."""
+    L = lib()
+    x = np.ascontiguousarray(x)
+    n = len(x)
+    nf_ = nfft or nperseg
+    _, S0 = framing(n, nperseg, noverlap, for_spectrogram=True)
+    F0 = nf_ // 2 + 1 if return_onesided else nf_
+    cap = max(S0 * F0, 1)
+    f = np.zeros(F0 + 1)
+    t = np.zeros(S0 + 1)
+    s = np.zeros(cap)
+    ns, nf = ctypes.c_int64(), ctypes.c_int64()
+    P = ctypes.POINTER(ctypes.c_double)
+    rc = L.ref_spectrogram(x.ctypes.data, n, _dt(x), fs, window.encode(), nperseg,
+                           noverlap, nfft, detrend.encode(), 1 if return_onesided else 0,
+                           mode.encode(), 1 if is_stft else 0, f.ctypes.data_as(P),
+                           t.ctypes.data_as(P), s.ctypes.data_as(P), cap,
+                           ctypes.byref(ns), ctypes.byref(nf))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    S, F = ns.value, nf.value
+    return f[:F].copy(), t[:S].copy(), s[:S * F].reshape(S, F).copy()
+
+
+def stft(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0):
+    return spectrogram(x, fs, window, nperseg, noverlap, nfft, is_stft=True)

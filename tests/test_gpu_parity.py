@@ -1,0 +1,295 @@
+"""Parity of the fused sm_100a kernels with the CPU oracle, through the C ABI.
+
+Every call goes through libinsight_b200_backend.so (insight_b200.signal is a
+ctypes mirror of the reference's Python API).  Tolerances are the parity bar:
+max_k |P - P_ref| / max_k |P_ref| <= 1e-5 for f32 and <= 1e-12 for f64;
+frequency and time axes and segment counts must be bit-exact.
+"""
+import numpy as np
+import pytest
+
+import insight_b200 as ib
+from oracle import spectral_oracle as so
+
+pytestmark = pytest.mark.gpu
+
+TOL = {np.float32: 1e-5, np.float64: 1e-12}
+
+
+def _sig(n, dtype, seed):
+    rng = np.random.default_rng(seed)
+    t = np.arange(n)
+    x = rng.standard_normal(n) + np.sin(2 * np.pi * 0.05 * t) + 0.5 * np.sin(
+        2 * np.pi * 0.31 * t)
+    return x.astype(dtype)
+
+
+def _np(a):
+    return a.detach().cpu().numpy() if hasattr(a, "detach") else np.asarray(a)
+
+
+def _to_gpu(x, cuda):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+
+
+# ---------------------------------------------------------------- welch ----
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("nperseg,nfft,window,detrend", [
+    (16, 0, "hann", "constant"),
+    (64, 0, "hamming", "constant"),
+    (256, 0, "hann", "constant"),
+    (1024, 0, "hann", "constant"),
+    (2048, 0, "blackman", "none"),
+    (4096, 0, "hamming", "linear"),
+    (8192, 0, "blackman", "constant"),
+    (100, 128, "hann", "constant"),     # zero padded, frequency-domain detrend
+    (200, 512, "hamming", "none"),
+])
+def test_welch(cuda, dtype, nperseg, nfft, window, detrend):
+    n = max(6 * nperseg + 37, 3000)
+    x = _sig(n, dtype, nperseg)
+    r = ib.welch(_to_gpu(x, cuda), fs=1e4, window=window, nperseg=nperseg,
+                 nfft=nfft, detrend=detrend)
+    f, p = so.welch(x, fs=1e4, window=window, nperseg=nperseg, nfft=nfft,
+                    detrend=detrend)
+    assert np.array_equal(_np(r.f), f)
+    assert so.max_rel_err(_np(r.Pxx), p) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("onesided,scaling,noverlap", [
+    (False, "density", 0), (True, "spectrum", 0), (True, "density", 200),
+    (False, "spectrum", 255)])
+def test_welch_options(cuda, dtype, onesided, scaling, noverlap):
+    x = _sig(5001, dtype, 7)
+    r = ib.welch(_to_gpu(x, cuda), fs=3.0, nperseg=256, noverlap=noverlap,
+                 return_onesided=onesided, scaling=scaling)
+    f, p = so.welch(x, fs=3.0, nperseg=256, noverlap=noverlap,
+                    return_onesided=onesided, scaling=scaling)
+    assert np.array_equal(_np(r.f), f)
+    assert so.max_rel_err(_np(r.Pxx), p) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_welch_host_arrays(dtype):
+    # numpy in, numpy out: the backend copies to and from the GPU itself.
+    x = _sig(1 << 16, dtype, 3)
+    r = ib.welch(x, fs=1e4, nperseg=1024, noverlap=512)
+    f, p = so.welch(x, fs=1e4, nperseg=1024, noverlap=512)
+    assert isinstance(r.Pxx, np.ndarray)
+    assert so.max_rel_err(r.Pxx, p) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("segments", [1, 2, 3, 17])
+def test_welch_segment_counts(cuda, segments):
+    # odd counts leave the last transform with a single segment
+    L = 256
+    n = (segments - 1) * 128 + L + 5
+    x = _sig(n, np.float64, segments)
+    r = ib.welch(_to_gpu(x, cuda), nperseg=L)
+    f, p = so.welch(x, nperseg=L)
+    assert so.max_rel_err(_np(r.Pxx), p) <= 1e-12
+
+
+# ------------------------------------------------------------------ csd ----
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("nperseg,nfft,detrend,onesided", [
+    (64, 0, "constant", True), (2048, 0, "constant", True),
+    (512, 0, "none", False), (300, 1024, "constant", True)])
+def test_csd(cuda, dtype, nperseg, nfft, detrend, onesided):
+    n = 9 * nperseg + 11
+    x = _sig(n, dtype, 1)
+    y = (0.7 * np.roll(x.astype(np.float64), 17) + 0.3 * _sig(n, np.float64, 2)
+         ).astype(dtype)
+    r = ib.csd(_to_gpu(x, cuda), _to_gpu(y, cuda), fs=2.0, nperseg=nperseg,
+               nfft=nfft, detrend=detrend, return_onesided=onesided)
+    f, p = so.csd(x, y, fs=2.0, nperseg=nperseg, nfft=nfft, detrend=detrend,
+                  return_onesided=onesided)
+    assert np.array_equal(_np(r.f), f)
+    assert so.max_rel_err(_np(r.Pxx), p) <= TOL[dtype]
+    # complex cross spectrum (native output)
+    f2, pc = ib.spectral(ib.OP_CSD, _to_gpu(x, cuda), _to_gpu(y, cuda), fs=2.0,
+                         nperseg=nperseg, nfft=nfft, detrend=detrend,
+                         return_onesided=onesided, complex_output=True)
+    _, pr = so.csd(x, y, fs=2.0, nperseg=nperseg, nfft=nfft, detrend=detrend,
+                   return_onesided=onesided, complex_output=True)
+    assert so.max_rel_err(_np(pc), pr) <= TOL[dtype]
+
+
+# ------------------------------------------------------ spectrogram/stft ----
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("mode", ["psd", "complex", "magnitude"])
+@pytest.mark.parametrize("nperseg,nfft,detrend", [
+    (128, 0, "constant"), (2048, 0, "none"), (96, 256, "constant")])
+def test_spectrogram(cuda, dtype, mode, nperseg, nfft, detrend):
+    n = 11 * nperseg + 3
+    x = _sig(n, dtype, 5)
+    r = ib.spectrogram(_to_gpu(x, cuda), fs=8.0, nperseg=nperseg, nfft=nfft,
+                       detrend=detrend, mode=mode)
+    f, t, s = so.spectrogram(x, fs=8.0, nperseg=nperseg, nfft=nfft,
+                             detrend=detrend, mode=mode)
+    assert np.array_equal(_np(r.f), f) and np.array_equal(_np(r.t), t)
+    assert _np(r.Sxx).shape == s.shape
+    assert so.max_rel_err(_np(r.Sxx), s) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("nperseg,noverlap", [(2048, 1536), (512, 0), (1024, 1000)])
+def test_stft(cuda, dtype, nperseg, noverlap):
+    x = _sig(40 * nperseg + 1, dtype, 9)
+    r = ib.stft(_to_gpu(x, cuda), fs=1e3, nperseg=nperseg, noverlap=noverlap)
+    f, t, s = so.stft(x, fs=1e3, nperseg=nperseg, noverlap=noverlap)
+    assert np.array_equal(_np(r.t), t)
+    assert so.max_rel_err(_np(r.Sxx), s) <= TOL[dtype]
+    rc = ib.stft(_to_gpu(x, cuda), fs=1e3, nperseg=nperseg, noverlap=noverlap,
+                 complex_output=True)
+    _, _, z = so.stft(x, fs=1e3, nperseg=nperseg, noverlap=noverlap,
+                      complex_output=True)
+    got = _np(rc.Sxx)
+    assert got.dtype == (np.complex64 if dtype == np.float32 else np.complex128)
+    assert so.max_rel_err(got, z) <= TOL[dtype]
+
+
+# ------------------------------------------------------ batched / strides ----
+@pytest.mark.parametrize("layout", ["rows", "transposed_view", "interleaved"])
+def test_batched_layouts(cuda, layout):
+    import torch
+    C, N, L = 6, 20000, 512
+    rng = np.random.default_rng(11)
+    X = rng.standard_normal((C, N)).astype(np.float32)
+    if layout == "rows":            # (C, N) contiguous, samples along axis 1
+        xt, axis = _to_gpu(X, cuda), -1
+    elif layout == "transposed_view":  # (N, C) view with strides (1, N)
+        xt, axis = _to_gpu(X, cuda).t(), 0
+    else:                           # (N, C) contiguous: sample stride C
+        xt, axis = _to_gpu(X.T.copy(), cuda), 0
+    f, p = ib.spectral(ib.OP_WELCH, xt, nperseg=L, axis=axis, fs=2.0)
+    p = _np(p)
+    assert p.shape == (C, L // 2 + 1)
+    for c in range(C):
+        _, pr = so.welch(X[c], fs=2.0, nperseg=L)
+        assert so.max_rel_err(p[c], pr) <= 1e-5
+    f, t, z = ib.spectral(ib.OP_STFT, xt, nperseg=L, noverlap=384, axis=axis,
+                          complex_output=True)
+    z = _np(z)
+    assert z.shape[:2] == (C, L // 2 + 1)
+    for c in (0, C - 1):
+        _, _, zr = so.stft(X[c], nperseg=L, noverlap=384, complex_output=True)
+        assert so.max_rel_err(z[c], zr) <= 1e-5
+    # csd of the same view against a shifted copy
+    Y = np.roll(X, 5, axis=1)
+    if layout == "rows":
+        yt = _to_gpu(Y, cuda)
+    elif layout == "transposed_view":
+        yt = _to_gpu(Y, cuda).t()
+    else:
+        yt = _to_gpu(Y.T.copy(), cuda)
+    f, pc = ib.spectral(ib.OP_CSD, xt, yt, nperseg=L, axis=axis, complex_output=True)
+    pc = _np(pc)
+    for c in (0, 3):
+        _, pr = so.csd(X[c], Y[c], nperseg=L, complex_output=True)
+        assert so.max_rel_err(pc[c], pr) <= 1e-5
+    torch.cuda.synchronize()
+
+
+def test_storage_offset_view(cuda):
+    import torch
+    base = _to_gpu(_sig(50000, np.float64, 4), cuda)
+    view = base[1234:1234 + 30000:2]          # offset and stride 2
+    x = _np(view)
+    r = ib.welch(view, nperseg=1024)
+    _, p = so.welch(x, nperseg=1024)
+    assert so.max_rel_err(_np(r.Pxx), p) <= 1e-12
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------- segment-range shards + sums ----
+@pytest.mark.parametrize("op", ["welch", "csd"])
+@pytest.mark.parametrize("shards", [2, 3])
+def test_segment_range_sums(cuda, op, shards):
+    import torch
+    dtype = np.float64
+    L = 512
+    x = _sig(60 * L + 100, dtype, 21)
+    y = _sig(60 * L + 100, dtype, 22)
+    code = ib.OP_WELCH if op == "welch" else ib.OP_CSD
+    _, S, F = ib.spectral_shape(code, _to_gpu(x, cuda), nperseg=L)
+    total = None
+    for k in range(shards):
+        s0, s1 = S * k // shards, S * (k + 1) // shards
+        _, part = ib.spectral(code, _to_gpu(x, cuda),
+                              _to_gpu(y, cuda) if op == "csd" else None,
+                              nperseg=L, seg_range=(s0, s1), raw_sums=True)
+        total = part if total is None else total + part
+    ib.finalize_sums(code, total, S, "float64", nperseg=L)
+    torch.cuda.synchronize()
+    if op == "welch":
+        _, ref = so.welch(x, nperseg=L)
+    else:
+        _, ref = so.csd(x, y, nperseg=L, complex_output=True)
+    assert so.max_rel_err(_np(total), ref) <= 1e-12
+
+
+# ---------------------------------------------------------- plugin boundary ----
+def test_plugin_registry_kernels(cuda):
+    """InitPluginGPU registers the kernels; call "welch" through the registry
+    signature exactly as the reference core's ops().launch would."""
+    import ctypes
+    import torch
+    from insight_b200 import _abi
+    lib = _abi.lib()
+    reg = {}
+
+    @_abi.REGISTER_FN
+    def register(name, dev, dt, fn):
+        reg[(name.decode(), dev, dt)] = fn
+        return 0
+
+    iface = _abi.C_DeviceInterface()
+    iface.size = ctypes.sizeof(_abi.C_DeviceInterface)
+    params = _abi.CustomRuntimeParams()
+    params.size = ctypes.sizeof(_abi.CustomRuntimeParams)
+    params.interface = ctypes.pointer(iface)
+    params.register_kernel = register
+    assert lib.InitPluginGPU(ctypes.byref(params)) == 0
+    assert params.device_type == b"b200"
+    assert (params.version.major, params.version.minor) == (1, 0)
+    for name in ("welch", "csd", "spectrogram", "stft"):
+        for dt in (_abi.DT_F32, _abi.DT_F64):
+            assert (name, _abi.DEV_GPU, dt) in reg
+    assert iface.device_memory_allocate and iface.get_last_error
+
+    x = _sig(40000, np.float32, 8)
+    xt = _to_gpu(x, cuda)
+    L = 1024
+    win = so.get_window("hann", L)
+    scale = so.psd_scale(win.astype(np.float32).astype(np.float64), 1e4, "density")
+    out = torch.empty(L // 2 + 1, dtype=torch.float64, device=cuda)
+    xa, oa = _abi.from_torch(xt), _abi.from_torch(out)
+    wa = _abi.from_numpy(win)
+    i64 = lambda v: ctypes.c_int64(v)
+    i32 = lambda v: ctypes.c_int32(v)
+    vals = [i64(L), i64(L // 2), i64(L), i32(1), i32(1), ctypes.c_double(scale), i64(0)]
+    ins = (ctypes.c_void_p * 12)(
+        ctypes.addressof(oa), ctypes.addressof(xa), ctypes.addressof(xa),
+        ctypes.addressof(wa), *[ctypes.addressof(v) for v in vals], None)
+    outs = (ctypes.c_void_p * 2)(ctypes.addressof(oa), None)
+    fn = ctypes.cast(reg[("welch", _abi.DEV_GPU, _abi.DT_F32)], _abi.KERNEL_FN)
+    assert fn(ins, outs) == 0, _abi.last_error()
+    _, p = so.welch(x, fs=1e4, nperseg=L)
+    assert so.max_rel_err(_np(out), p) <= 1e-5
+    # a bad call fails with a message, never with C_FALLBACK (5)
+    bad = (ctypes.c_void_p * 3)(ctypes.addressof(oa), ctypes.addressof(xa), None)
+    assert fn(bad, outs) == _abi.C_FAILED
+    assert "expected" in _abi.last_error()
+
+
+def test_errors_match_reference(cuda):
+    x = _to_gpu(_sig(100, np.float64, 1), cuda)
+    with pytest.raises(RuntimeError, match="signal too short for given nperseg"):
+        ib.welch(x, nperseg=256)
+    with pytest.raises(RuntimeError, match="spectrogram: signal too short"):
+        ib.spectrogram(x, nperseg=256)
+    with pytest.raises(RuntimeError, match="unknown window name 'nope'"):
+        ib.welch(x, nperseg=16, window="nope")
