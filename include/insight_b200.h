@@ -375,6 +375,30 @@ INSIGHT_B200_API C_Status insight_b200_finalize_sums(
     const InsightB200SpectralDesc *desc, int64_t n_seg, int32_t x_dtype,
     InsightArray *sums, void *stream);
 
+/* Welch PSD without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot let a library allocate device
+ * memory, such as a host framework that hands out every GPU buffer from its
+ * own pool, or a latency-critical path that must not pay the implicit device
+ * synchronisation of cudaMalloc / cudaFree.
+ * x is a device pointer (current device) to sample 0 of channel 0, with
+ * element strides channel_stride / sample_stride; pxx is a device pointer to
+ * an F64 [n_channels, n_freq] contiguous result.  Arguments mean what they
+ * mean in insight_b200_welch.  The working memory (twiddles, window, partial
+ * sums) is an 8 MiB file-scope device array that every GPU loading this
+ * library holds until exit; calls needing more (n_channels * (nfft/2+1) * 8
+ * bytes beyond ~8 MiB) and constant detrend with nfft > nperseg are rejected
+ * with C_FAILED.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on a device share the array, so calls that overlap on
+ * the GPU race.  stream is a cudaStream_t (NULL: legacy default stream); the
+ * call returns after the stream has finished the work. */
+INSIGHT_B200_API C_Status insight_b200_welch_noalloc(
+    const void *x, int32_t dtype, int64_t n_channels, int64_t n_samples,
+    int64_t channel_stride, int64_t sample_stride, double fs,
+    const char *window, int64_t nperseg, int64_t noverlap, int64_t nfft,
+    const char *detrend, int32_t return_onesided, const char *scaling,
+    double *pxx, void *stream);
+
 /* Kernel launches issued by this process so far (all devices). */
 INSIGHT_B200_API int64_t insight_b200_launch_count(void);
 

@@ -116,6 +116,7 @@ EXPORTS = (
     "insight_b200_spectral",
     "insight_b200_finalize_sums",
     "insight_b200_launch_count",
+    "insight_b200_welch_noalloc",
 )
 
 _lib = None
@@ -158,6 +159,12 @@ def lib() -> ctypes.CDLL:
                                             ctypes.c_int]
         L.insight_b200_finalize_sums.argtypes = [PD, ctypes.c_int64, ctypes.c_int32,
                                                  PA, ctypes.c_void_p]
+        L.insight_b200_welch_noalloc.argtypes = [
+            ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+            ctypes.c_int64, ctypes.c_int64, ctypes.c_double, ctypes.c_char_p,
+            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_char_p,
+            ctypes.c_int32, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.insight_b200_welch_noalloc.restype = ctypes.c_int
         for n in ("insight_b200_welch", "insight_b200_csd", "insight_b200_spectrogram",
                   "insight_b200_stft", "insight_b200_spectral_shape",
                   "insight_b200_spectral", "insight_b200_finalize_sums"):

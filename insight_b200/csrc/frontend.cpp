@@ -41,6 +41,7 @@ std::atomic<int64_t> g_launches{0};
 void set_last_error(const std::string &msg) { g_last_error = msg; }
 const char *last_error() { return g_last_error.c_str(); }
 int64_t launch_count() { return g_launches.load(); }
+void add_launches(int64_t n) { g_launches += n; }
 
 struct Fail : std::runtime_error {
   using std::runtime_error::runtime_error;

@@ -45,5 +45,6 @@ C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums);
 void set_last_error(const std::string &msg);
 const char *last_error();
 int64_t launch_count();
+void add_launches(int64_t n);
 
 } // namespace ib200

@@ -22,6 +22,8 @@ AccSplit acc_split(const LaunchDesc &d, int num_sms, int blocks_per_sm) {
   q0 = std::max<int64_t>(q0, std::min<int64_t>(s.Tc, 16));
   q0 = std::max<int64_t>(q0, 1);
   s.nq = (s.Tc + q0 - 1) / q0;
+  if (d.max_units > 0 && d.C * s.nq > d.max_units)
+    s.nq = std::max<int64_t>(1, d.max_units / std::max<int64_t>(d.C, 1));
   s.Qt = (s.Tc + s.nq - 1) / s.nq;
   s.U = d.C * s.nq;
   const int64_t gmax = (int64_t)std::max(num_sms, 1) * std::max(blocks_per_sm, 1);

@@ -41,6 +41,7 @@ struct LaunchDesc {
   void *out = nullptr;
   int64_t o_cs = 0, o_rs = 0, o_ts = 0; // elements
   double psd_scale = 1.0;     // spectrogram 'psd'
+  int64_t max_units = 0;      // welch / csd: cap on work units (0 = none)
 };
 
 // Bytes of scratch the launch needs (welch / csd unit partials).
