@@ -122,13 +122,16 @@ template <int R> __host__ __device__ constexpr int bitrev(int v) {
   return r;
 }
 
-// In-register R-point forward DFT, natural order in and out.
+// In-register R-point forward DFT: natural-order input, output in
+// bit-reversed register order (a[i] = X[bitrev(i)]); consumers index with
+// bitrev<R>() at compile time instead of moving registers.
 template <typename T, int R, typename V>
 __device__ __forceinline__ void dft_reg(V *a) {
   static_assert(R >= 1 && R <= 32 && (R & (R - 1)) == 0, "radix");
   if constexpr (R > 1) {
     // radix-2 DIF network: span H = R/2, R/4, ..., 1
-    static_for<0, 32>([&](auto sIC) {
+    constexpr int STAGES = R == 2 ? 1 : R == 4 ? 2 : R == 8 ? 3 : R == 16 ? 4 : 5;
+    static_for<0, STAGES>([&](auto sIC) {
       constexpr int s = decltype(sIC)::value;
       constexpr int H = R >> (s + 1);
       if constexpr (H >= 1) {
@@ -142,15 +145,6 @@ __device__ __forceinline__ void dft_reg(V *a) {
           });
         });
       }
-    });
-    V t[R];
-    static_for<0, R>([&](auto kIC) {
-      constexpr int k = decltype(kIC)::value;
-      t[k] = a[bitrev<R>(k)];
-    });
-    static_for<0, R>([&](auto kIC) {
-      constexpr int k = decltype(kIC)::value;
-      a[k] = t[k];
     });
   }
 }
@@ -235,7 +229,16 @@ __device__ __forceinline__ void pass_compute(V *v, int t, const V *tw) {
   });
 }
 
-// Write the outputs of pass PASS to shared memory.
+// Padded offset of a compile-time distance D from an index whose padding is
+// already accounted for: valid when D is a multiple of 16.
+template <int D> __host__ __device__ constexpr int pad_off() {
+  static_assert(D % 16 == 0, "padded offsets need multiples of 16");
+  return D + D / 16;
+}
+
+// Write the outputs of pass PASS to shared memory.  Element r of butterfly j
+// goes to base + r*NS; with NS == 1 the base is a multiple of R <= 16 so the
+// whole run shares one pad slot, with NS % 16 == 0 every step is D = NS.
 template <int L, int E, int P, int PASS, typename V>
 __device__ __forceinline__ void pass_store(const V *v, V *buf, int t) {
   using PL = Plan<L, E>;
@@ -247,14 +250,28 @@ __device__ __forceinline__ void pass_store(const V *v, V *buf, int t) {
     const int j = t + b * P;
     const int k = j & (NS - 1);
     const int base = (j / NS) * NS * R + k;
-    static_for<0, R>([&](auto rIC) {
-      constexpr int r = decltype(rIC)::value;
-      buf[spad(base + r * NS)] = v[b * R + r];
-    });
+    if constexpr (NS == 1 && R <= 16) {
+      V *q = buf + spad(base);
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        q[r] = v[b * R + bitrev<R>(r)];
+      });
+    } else if constexpr (NS % 16 == 0) {
+      V *q = buf + spad(base);
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        q[pad_off<r * NS>()] = v[b * R + bitrev<R>(r)];
+      });
+    } else {
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        buf[spad(base + r * NS)] = v[b * R + bitrev<R>(r)];
+      });
+    }
   });
 }
 
-// Read the inputs of pass PASS from shared memory.
+// Read the inputs of pass PASS from shared memory (stride L/R).
 template <int L, int E, int P, int PASS, typename V>
 __device__ __forceinline__ void pass_load(V *v, const V *buf, int t) {
   using PL = Plan<L, E>;
@@ -263,17 +280,230 @@ __device__ __forceinline__ void pass_load(V *v, const V *buf, int t) {
   static_for<0, B>([&](auto bIC) {
     constexpr int b = decltype(bIC)::value;
     const int j = t + b * P;
-    static_for<0, R>([&](auto rIC) {
-      constexpr int r = decltype(rIC)::value;
-      v[b * R + r] = buf[spad(j + r * (L / R))];
+    if constexpr ((L / R) % 16 == 0) {
+      const V *q = buf + spad(j);
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        v[b * R + r] = q[pad_off<r * (L / R)>()];
+      });
+    } else {
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        v[b * R + r] = buf[spad(j + r * (L / R))];
+      });
+    }
+  });
+}
+
+// Write the transform (natural order, as left by fft_group) to shared memory.
+template <int L, int E, int P, typename V>
+__device__ __forceinline__ void store_bins(const V *v, V *buf, int t) {
+  constexpr int R = Plan<L, E>::radix(Plan<L, E>::passes() - 1);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    const int j = t + b * P;
+    if constexpr ((L / R) % 16 == 0) {
+      V *q = buf + spad(j);
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        q[pad_off<r * (L / R)>()] = v[b * R + bitrev<R>(r)];
+      });
+    } else {
+      static_for<0, R>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        buf[spad(j + r * (L / R))] = v[b * R + bitrev<R>(r)];
+      });
+    }
+  });
+}
+
+// Per-thread Stockham twiddles.  A thread's butterflies j = t + b*P have the
+// same k = j mod NS in every transform, so the R-1 factors W_{NS*R}^{r*k} of
+// each pass p >= 1 are loop invariant.  They are read once per CTA from the
+// W_L table into a shared-memory row per thread: butterfly (p, b) owns R
+// slots (r = 1..R-1 and one pad) at offset(p) + b*R, so every pair of slots
+// is 16-byte aligned.  Row strides keep 128-bit reads bank-conflict free.
+template <typename T, int L, int E> struct ThreadTw {
+  using PL = Plan<L, E>;
+  __host__ __device__ static constexpr int block(int p) {
+    return (E / PL::radix(p)) * PL::radix(p);
+  }
+  __host__ __device__ static constexpr int offset(int p) {
+    int o = 0;
+    for (int q = 1; q < p; ++q)
+      o += block(q);
+    return o;
+  }
+  __host__ __device__ static constexpr int total() {
+    return offset(PL::passes());
+  }
+  __host__ __device__ static constexpr int stride() {
+    // f32 entries are 8 bytes: stride = 2 (mod 4) keeps eight 16-byte lanes
+    // on distinct bank quads; f64 entries are 16 bytes: an odd stride.
+    if (sizeof(T) == 4) {
+      int s = total() + 2;
+      while (s % 4 != 2)
+        ++s;
+      return s;
+    }
+    return total() | 1;
+  }
+};
+
+template <typename T, int L, int E, int P, typename V>
+__device__ __forceinline__ void fill_thread_twiddles(V *tws, const V *tw,
+                                                     int tid, int nthreads) {
+  using PL = Plan<L, E>;
+  using TT = ThreadTw<T, L, E>;
+  constexpr int NPASS = PL::passes();
+  for (int i = tid; i < P * TT::total(); i += nthreads) {
+    const int tt = i / TT::total();
+    int slot = i - tt * TT::total();
+    V val = {T(1), T(0)};
+    static_for<1, NPASS>([&](auto pIC) {
+      constexpr int p = decltype(pIC)::value;
+      constexpr int R = PL::radix(p);
+      constexpr int NS = PL::ns(p);
+      if (slot >= TT::offset(p) && slot < TT::offset(p) + TT::block(p)) {
+        const int rel = slot - TT::offset(p);
+        const int b = rel / R;
+        const int r = rel - b * R + 1; // slot R-1 of a butterfly is padding
+        if (r < R) {
+          const int k = (tt + b * P) & (NS - 1);
+          val = tw[((int64_t)r * k * (L / (NS * R))) % L];
+        }
+      }
     });
+    tws[tt * TT::stride() + slot] = val;
+  }
+}
+
+// pass_compute with the per-thread twiddle row instead of the recurrence.
+template <typename T, int L, int E, int P, int PASS, typename V>
+__device__ __forceinline__ void pass_compute_tw(V *v, const V *row) {
+  using PL = Plan<L, E>;
+  using TT = ThreadTw<T, L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int NS = PL::ns(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    if constexpr (NS > 1) {
+      const V *w = row + TT::offset(PASS) + b * R;
+      if constexpr (sizeof(T) == 4) {
+        static_for<0, R / 2>([&](auto qIC) {
+          constexpr int q = decltype(qIC)::value;
+          const float4 f = reinterpret_cast<const float4 *>(w)[q];
+          const V w0 = {f.x, f.y}, w1 = {f.z, f.w};
+          // slots 2q, 2q+1 hold r = 2q+1, 2q+2
+          v[b * R + 2 * q + 1] = vmul(v[b * R + 2 * q + 1], w0);
+          if constexpr (2 * q + 2 < R)
+            v[b * R + 2 * q + 2] = vmul(v[b * R + 2 * q + 2], w1);
+        });
+      } else {
+        static_for<1, R>([&](auto rIC) {
+          constexpr int r = decltype(rIC)::value;
+          v[b * R + r] = vmul(v[b * R + r], w[r - 1]);
+        });
+      }
+    }
+    dft_reg<T, R>(v + b * R);
+  });
+}
+
+// fft_group with per-thread twiddles (row = this thread's twiddle row).
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group_tw(V *v, V *buf, int t, int g,
+                                             const V *row) {
+  constexpr int NP = Plan<L, E>::passes();
+  static_for<0, NP>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+    pass_compute_tw<T, L, E, P, p>(v, row);
+    if constexpr (p + 1 < NP) {
+      pass_store<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+  });
+}
+
+// M independent transforms per thread (v[m][E], buffer of transform m at
+// buf + m * bstride), sharing the per-thread twiddle loads and the barriers;
+// the two instruction streams interleave and hide each other's latency.
+template <typename T, int L, int E, int P, int PASS, int M, typename V>
+__device__ __forceinline__ void pass_compute_tw_m(V (*v)[E], const V *row) {
+  using PL = Plan<L, E>;
+  using TT = ThreadTw<T, L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int NS = PL::ns(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    if constexpr (NS > 1) {
+      const V *w = row + TT::offset(PASS) + b * R;
+      static_for<0, R / 2>([&](auto qIC) {
+        constexpr int q = decltype(qIC)::value;
+        V w0, w1;
+        if constexpr (sizeof(T) == 4) {
+          const float4 f = reinterpret_cast<const float4 *>(w)[q];
+          w0 = {f.x, f.y};
+          w1 = {f.z, f.w};
+        } else {
+          w0 = w[2 * q];
+          w1 = w[2 * q + 1];
+        }
+        static_for<0, M>([&](auto mIC) {
+          constexpr int m = decltype(mIC)::value;
+          v[m][b * R + 2 * q + 1] = vmul(v[m][b * R + 2 * q + 1], w0);
+          if constexpr (2 * q + 2 < R)
+            v[m][b * R + 2 * q + 2] = vmul(v[m][b * R + 2 * q + 2], w1);
+        });
+      });
+    }
+    static_for<0, M>([&](auto mIC) {
+      constexpr int m = decltype(mIC)::value;
+      dft_reg<T, R>(v[m] + b * R);
+    });
+  });
+}
+
+// SKIP0: pass 0 (which reads only registers) was already computed by the
+// caller, e.g. overlapped with other work.
+template <typename T, int L, int E, int P, int G, int M, bool SKIP0 = false,
+          typename V>
+__device__ __forceinline__ void fft_group_tw_m(V (*v)[E], V *buf, int bstride,
+                                               int t, int g, const V *row) {
+  constexpr int NP = Plan<L, E>::passes();
+  static_for<0, NP>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0) {
+      static_for<0, M>([&](auto mIC) {
+        constexpr int m = decltype(mIC)::value;
+        pass_load<L, E, P, p>(v[m], buf + m * bstride, t);
+      });
+      group_sync<G, P>(g);
+    }
+    if constexpr (p > 0 || !SKIP0)
+      pass_compute_tw_m<T, L, E, P, p, M>(v, row);
+    if constexpr (p + 1 < NP) {
+      static_for<0, M>([&](auto mIC) {
+        constexpr int m = decltype(mIC)::value;
+        pass_store<L, E, P, p>(v[m], buf + m * bstride, t);
+      });
+      group_sync<G, P>(g);
+    }
   });
 }
 
 // Full transform after pass 0's inputs are in registers.  On return v holds
 // the DFT: v[b*R + r] = X[t + b*P + r*(L/R)] with R the last radix.
 // buf is the group's padded buffer (spad_size(L) values).
-template <typename T, int L, int E, int P, int G, typename V>
+template <typename T, int L, int E, int P, int G, bool SKIP0 = false,
+          typename V>
 __device__ __forceinline__ void fft_group(V *v, V *buf, int t, int g,
                                           const V *tw) {
   constexpr int NP = Plan<L, E>::passes();
@@ -283,7 +513,8 @@ __device__ __forceinline__ void fft_group(V *v, V *buf, int t, int g,
       pass_load<L, E, P, p>(v, buf, t);
       group_sync<G, P>(g); // every read of this pass done before rewriting
     }
-    pass_compute<T, L, E, P, p>(v, t, tw);
+    if constexpr (p > 0 || !SKIP0)
+      pass_compute<T, L, E, P, p>(v, t, tw);
     if constexpr (p + 1 < NP) {
       pass_store<L, E, P, p>(v, buf, t);
       group_sync<G, P>(g);
@@ -291,16 +522,36 @@ __device__ __forceinline__ void fft_group(V *v, V *buf, int t, int g,
   });
 }
 
-// Position (natural-order bin) of register slot e after fft_group.
+// Every pass but the last, leaving the input of the last pass in buf (stored,
+// not yet synchronised: the caller synchronises before reading it).
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group_prefix(V *v, V *buf, int t, int g,
+                                                 const V *tw) {
+  constexpr int NP = Plan<L, E>::passes();
+  static_for<0, NP - 1>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+    pass_compute<T, L, E, P, p>(v, t, tw);
+    pass_store<L, E, P, p>(v, buf, t);
+    if constexpr (p + 2 < NP)
+      group_sync<G, P>(g);
+  });
+}
+
+// Position (natural-order bin) of register slot e after fft_group (the last
+// pass leaves each butterfly's outputs in bit-reversed register order).
 template <int L, int E, int P>
-__device__ __forceinline__ int out_bin(int t, int e) {
+__host__ __device__ constexpr int out_bin(int t, int e) {
   constexpr int R = Plan<L, E>::radix(Plan<L, E>::passes() - 1);
-  return t + (e / R) * P + (e % R) * (L / R);
+  return t + (e / R) * P + bitrev<R>(e % R) * (L / R);
 }
 
 // Position (time index) of register slot e for pass-0 inputs.
 template <int L, int E, int P>
-__device__ __forceinline__ int in_index(int t, int e) {
+__host__ __device__ constexpr int in_index(int t, int e) {
   constexpr int R = Plan<L, E>::radix(0);
   return t + (e / R) * P + (e % R) * (L / R);
 }

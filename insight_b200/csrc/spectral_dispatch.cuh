@@ -38,6 +38,78 @@ template <typename T> __host__ __device__ constexpr int store_groups(int L) {
   return g;
 }
 
+// Shared-memory budget of one CTA of the STFT fast path.
+#ifndef IB200_STFT_SMEM_BUDGET
+#define IB200_STFT_SMEM_BUDGET 225280
+#endif
+
+// Fast-path shape: G transform groups per CTA, M interleaved transforms per
+// thread, and whether the per-thread twiddle rows fit in shared memory.  The
+// preferred shape is IB200_STFT_PAIRS segment pairs per tile (8 pairs give
+// 16-segment, 128-byte complex64 runs per bin row) with IB200_STFT_INTERLEAVE
+// transforms per thread.
+template <typename T> struct FastShape {
+  int G, M;
+  bool tws;
+};
+
+#ifndef IB200_STFT_PAIRS
+#define IB200_STFT_PAIRS 8
+#endif
+#ifndef IB200_STFT_INTERLEAVE
+#define IB200_STFT_INTERLEAVE 1
+#endif
+
+template <typename T, int L>
+constexpr size_t fast_smem_bytes(int G, int M, bool tws) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr int SEC = 32 / (2 * (int)sizeof(T));
+  size_t b = (size_t)G * M * (spad_size(L) + 2) * 2 * sizeof(T) +
+             (size_t)P * (E + 16 / sizeof(T)) * sizeof(T) +
+             ((size_t)(L / 2 + 1) * (SEC - 1) * 2 * sizeof(T) + 15) / 16 * 16;
+  if (tws)
+    b += (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T);
+  return b;
+}
+
+template <typename T, int L> constexpr FastShape<T> fast_shape_any() {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  if (P % 32 != 0)
+    return {0, 0, false};
+  // interleaved: Q pairs as Q/M groups of M transforms, twiddle rows required
+  for (int q = IB200_STFT_PAIRS; q >= 4; q /= 2) {
+    const int m = IB200_STFT_INTERLEAVE;
+    const int g = q / m;
+    if (g >= 1 && g * P <= 1024 && (g * P) / (2 * q) >= 16 &&
+        ((g * P) / (2 * q)) % 16 == 0 &&
+        fast_smem_bytes<T, L>(g, m, true) <= IB200_STFT_SMEM_BUDGET)
+      return {g, m, true};
+  }
+  // one transform per thread
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool tws = pass == 0;
+    int g = 8;
+    while (g > 1 && (fast_smem_bytes<T, L>(g, 1, tws) > IB200_STFT_SMEM_BUDGET ||
+                     g * P > 1024))
+      g /= 2;
+    if (fast_smem_bytes<T, L>(g, 1, tws) <= IB200_STFT_SMEM_BUDGET &&
+        (g >= 4 || !tws) && P / 2 >= 16)
+      return {g, 1, tws};
+  }
+  return {0, 0, false};
+}
+
+// The sector-aligned store needs tile rows of whole 32-byte sectors.
+template <typename T, int L> constexpr FastShape<T> fast_shape() {
+  constexpr FastShape<T> s = fast_shape_any<T, L>();
+  constexpr int sec = 32 / (2 * (int)sizeof(T));
+  if (s.G == 0 || 2 * s.G * s.M < sec || (2 * s.G * s.M) % sec != 0)
+    return {0, 0, false};
+  return s;
+}
+
 template <typename T>
 SpecArgs<T> make_args(const LaunchDesc &d, void *scratch) {
   using V = typename V2T<T>::type;
@@ -110,10 +182,89 @@ cudaError_t run_accum(const LaunchDesc &d, void *scratch, int num_sms,
   return cudaGetLastError();
 }
 
+// Overlap shift of the fast path: hop = SH * L/R0 with SH in {R0/4, R0/2}
+// (75% / 50% overlap) reuses registers; other hops load both segments.
+template <typename T, int L> int fast_shift(int64_t step) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int R0 = Plan<L, E>::radix(0);
+  constexpr int Q = L / R0;
+  if (step % Q != 0)
+    return 0;
+  const int64_t sh = step / Q;
+  if (R0 >= 4 && sh == R0 / 4)
+    return R0 / 4;
+  if (R0 >= 2 && sh == R0 / 2)
+    return R0 / 2;
+  return 0;
+}
+
+template <typename T, int L, int SH>
+cudaError_t run_stft_fast_sh(const LaunchDesc &d, int num_sms,
+                             cudaStream_t stream, int64_t *launches) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr FastShape<T> FS = fast_shape<T, L>();
+  constexpr int G = FS.G;
+  constexpr int M = FS.M;
+  auto kern = stft_fast_kernel<T, L, E, G, M, SH, FS.tws>;
+  const size_t smem = fast_smem_bytes<T, L>(G, M, FS.tws);
+  static int blocks_per_sm = -1;
+  if (blocks_per_sm < 0) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+      return e;
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G * P, smem);
+    if (e != cudaSuccess)
+      return e;
+    blocks_per_sm = std::max(nb, 1);
+  }
+  SpecArgs<T> a = make_args<T>(d, nullptr);
+  // Units of nsub consecutive tiles per CTA: long enough that the partial
+  // sectors at unit ends are a few percent of the writes, short enough for
+  // about eight units per resident CTA.
+  const int64_t tpc = (a.Tc + G * M - 1) / (G * M);
+  const int64_t ctas = (int64_t)num_sms * blocks_per_sm;
+  int nsub = (int)std::max<int64_t>(
+      1, std::min<int64_t>(16, (d.C * tpc) / std::max<int64_t>(1, 8 * ctas)));
+  const int64_t units = d.C * ((tpc + nsub - 1) / nsub);
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units, ctas));
+  kern<<<(unsigned)grid, G * P, smem, stream>>>(a, nsub);
+  if (launches)
+    *launches += 1;
+  return cudaGetLastError();
+}
+
+template <typename T, int L>
+cudaError_t run_stft_fast(const LaunchDesc &d, int num_sms, cudaStream_t stream,
+                          int64_t *launches) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int R0 = Plan<L, E>::radix(0);
+  const int sh = fast_shift<T, L>(d.step);
+  if constexpr (R0 >= 4) {
+    if (sh == R0 / 4)
+      return run_stft_fast_sh<T, L, R0 / 4>(d, num_sms, stream, launches);
+  }
+  if constexpr (R0 >= 2) {
+    if (sh == R0 / 2)
+      return run_stft_fast_sh<T, L, R0 / 2>(d, num_sms, stream, launches);
+  }
+  return run_stft_fast_sh<T, L, 0>(d, num_sms, stream, launches);
+}
+
 template <typename T, int L>
 cudaError_t run_store(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                       int64_t *launches) {
   using V = typename V2T<T>::type;
+  constexpr int EE = values_per_thread<T>(L);
+  if constexpr (fast_shape<T, L>().G > 0 && Plan<L, EE>::passes() >= 2) {
+    const bool want = std::is_same<T, float>::value ? d.out_kind == OUT_C64_K
+                                                    : d.out_kind == OUT_C128_K;
+    if (want && d.x_ss == 1 && d.nperseg == d.nfft && d.dc_mode <= 1 &&
+        d.o_ts == 1 && d.F == d.nfft / 2 + 1)
+      return run_stft_fast<T, L>(d, num_sms, stream, launches);
+  }
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   constexpr int G = store_groups<T>(L);

@@ -145,9 +145,7 @@ __global__ void __launch_bounds__(L / E)
         for (int e = 0; e < E; ++e)
           acc[e] += (double)fma(v[e].x, v[e].x, v[e].y * v[e].y);
       } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e)
-          buf[spad(out_bin<L, E, P>(t, e))] = v[e];
+        store_bins<L, E, P>(v, buf, t);
         __syncthreads();
         V m = {T(0), T(0)};
         if (p.dc_mode == 2) {
@@ -291,9 +289,7 @@ __global__ void __launch_bounds__(G *(L / E))
                             xc + (s + 1) * p.step * p.x_ss, p.x_ss, p.x_ss,
                             hasb, p.nperseg, p.win, t);
       fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        buf[spad(out_bin<L, E, P>(t, e))] = v[e];
+      store_bins<L, E, P>(v, buf, t);
     }
     __syncthreads();
 
@@ -357,6 +353,233 @@ __global__ void __launch_bounds__(G *(L / E))
       }
     }
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// STFT fast path: contiguous channels (unit sample stride), nperseg == nfft,
+// one-sided, no detrend or DC-only detrend, complex<T> output (C, F, S) with
+// unit segment stride.
+//
+// Work unit: NSUB consecutive tiles of one channel, one CTA.  A tile is Q =
+// G*M consecutive segment pairs; each of the G transform groups (P threads)
+// runs M pairs at once, interleaved in registers.
+//   * loads: with SH > 0 the second segment's samples that overlap the first
+//     come from the first segment's registers (hop = SH * L/R0);
+//   * the window rows (pre-scaled by 1/2, the unpack factor; exact in binary
+//     floating point) and, with TWS, each thread's Stockham twiddles live in
+//     shared memory, filled once per CTA;
+//   * the transforms are staged in shared memory; the whole CTA then unpacks
+//     A[k] = Z[k] + conj Z[L-k], B[k] = -i (Z[k] - conj Z[L-k]) (halves folded
+//     into the window), 2Q lanes per bin row.
+// Bin rows of the (C, F, S) output start at arbitrary element offsets (S is
+// odd in general), so a tile's 2Q columns do not cover whole 32-byte
+// sectors; sectors completed by two CTAs become masked DRAM writes.  The
+// lanes of a row therefore write the 2Q columns that end on a sector
+// boundary, shifted back by the row's phase phi, and keep the phi trailing
+// columns in a per-row carry for the unit's next tile: every sector of a
+// row is written once, whole, except at the two ends of a unit.
+// ---------------------------------------------------------------------------
+template <typename T, int L, int E, int G, int M, int SH, bool TWS>
+__global__ void __launch_bounds__(G *(L / E))
+    stft_fast_kernel(const SpecArgs<T> p, int nsub) {
+  using V = typename V2T<T>::type;
+  using PL = Plan<L, E>;
+  using TT = ThreadTw<T, L, E>;
+  constexpr int P = L / E;
+  constexpr int NT = G * P;
+  constexpr int Q = G * M;               // segment pairs per tile
+  constexpr int R0 = PL::radix(0);
+  constexpr int GS = spad_size(L) + 2;   // slot spad(L) holds a copy of Z[0]
+  constexpr int SPR = 2 * Q;             // columns (segments) per tile row
+  constexpr int RPI = NT / SPR;          // bin rows per store iteration
+  constexpr int FH = L / 2 + 1;
+  constexpr int NIT = (FH + RPI - 1) / RPI;
+  constexpr int WS = E + 16 / (int)sizeof(T);
+  constexpr int SEC = 32 / (int)sizeof(V); // output values per 32-byte sector
+  // carry slots, rounded to 16 bytes so the window rows after them stay
+  // aligned for 128-bit reads
+  constexpr int CN = (FH * (SEC - 1) * (int)sizeof(V) + 15) / 16 * 16 / (int)sizeof(V);
+  static_assert(SPR % SEC == 0 && SPR >= SEC, "tile rows are whole sectors");
+  static_assert(SH >= 0 && SH < R0, "overlap shift");
+  static_assert(TWS || M == 1, "interleaved transforms use twiddle rows");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  V *smem = reinterpret_cast<V *>(smem_raw);
+  V *tws = smem + Q * GS;                                   // [P][stride]
+  V *carry = tws + (TWS ? P * TT::stride() : 0);            // [FH][SEC-1]
+  T *wsm = reinterpret_cast<T *>(carry + CN);                // [P][WS]
+  const int g = threadIdx.x / P;
+  const int t = threadIdx.x - g * P;
+  V *buf = smem + g * M * GS; // pairs g*M .. g*M + M - 1
+
+  for (int i = threadIdx.x; i < P * E; i += NT) {
+    const int tt = i / E, e = i - tt * E;
+    wsm[tt * WS + e] = T(0.5) * p.win[in_index<L, E, P>(tt, e)];
+  }
+  if constexpr (TWS)
+    fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+  __syncthreads();
+  const V *row = tws + t * TT::stride();
+
+  const int lane = threadIdx.x % SPR;
+  const int kr0 = threadIdx.x / SPR;
+  static_assert(RPI % SEC == 0, "a thread's rows share one sector phase");
+
+  const int64_t tpc = (p.Tc + Q - 1) / Q;       // tiles per channel
+  const int64_t upc = (tpc + nsub - 1) / nsub;  // units per channel
+  const int64_t nunits = p.C * upc;
+  V *out = reinterpret_cast<V *>(p.out);
+
+  // Windowed inputs of the group's M pairs of a tile into v; false when the
+  // group's first pair is past the channel's end (the whole group idles).
+  V v[M][E];
+  auto load_tile = [&](int64_t c, int64_t task0) -> bool {
+    const int64_t taskg = task0 + g * M;
+    if (taskg >= p.Tc)
+      return false;
+    T wv[E];
+    if constexpr (sizeof(T) == 4 && E % 4 == 0) {
+      const float4 *w4 = reinterpret_cast<const float4 *>(wsm + t * WS);
+      static_for<0, E / 4>([&](auto qIC) {
+        constexpr int q = decltype(qIC)::value;
+        const float4 f = w4[q];
+        wv[4 * q] = f.x;
+        wv[4 * q + 1] = f.y;
+        wv[4 * q + 2] = f.z;
+        wv[4 * q + 3] = f.w;
+      });
+    } else if constexpr (sizeof(T) == 8 && E % 2 == 0) {
+      const double2 *w2 = reinterpret_cast<const double2 *>(wsm + t * WS);
+      static_for<0, E / 2>([&](auto qIC) {
+        constexpr int q = decltype(qIC)::value;
+        const double2 f = w2[q];
+        wv[2 * q] = f.x;
+        wv[2 * q + 1] = f.y;
+      });
+    } else {
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        wv[e] = wsm[t * WS + e];
+      });
+    }
+    static_for<0, M>([&](auto mIC) {
+      constexpr int m = decltype(mIC)::value;
+      const int64_t task = taskg + m;
+      // a missing pair (channel tail) transforms zeros, never stored
+      const bool hasa = task < p.Tc;
+      const bool hasb = (2 * task + 1) < p.S;
+      const T *xa = p.x + c * p.x_cs +
+                    (p.seg0 + 2 * (hasa ? task : taskg)) * p.step + t;
+      if (!hasa) {
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          v[m][e] = {T(0), T(0)};
+        });
+        return;
+      }
+      T ra[E];
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        ra[e] = __ldg(xa + in_index<L, E, P>(0, e));
+      });
+      if (hasb) {
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          constexpr int n = in_index<L, E, P>(0, e);
+          constexpr int r = e % R0;
+          T b;
+          if constexpr (SH > 0 && r + SH < R0)
+            b = ra[e + SH];
+          else
+            b = __ldg(xa + p.step + n);
+          v[m][e] = {ra[e] * wv[e], b * wv[e]};
+        });
+      } else {
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          v[m][e] = {ra[e] * wv[e], T(0)};
+        });
+      }
+    });
+    return true;
+  };
+  for (int64_t unit = blockIdx.x; unit < nunits; unit += gridDim.x) {
+    const int64_t c = unit / upc;
+    const int64_t tile0 = (unit - c * upc) * nsub;
+    const int ntile = (int)min((int64_t)nsub, tpc - tile0);
+    const int64_t ucol0 = 2 * tile0 * Q; // first column of the unit
+    V *outc = out + c * p.o_cs;
+    // this thread's store role for the unit (see the store below)
+    const int phi = (int)((reinterpret_cast<uint64_t>(outc + (int64_t)kr0 * p.o_rs +
+                                                       ucol0) /
+                           sizeof(V)) & (SEC - 1));
+    const bool carry_lane = lane < phi;
+    const int jj = carry_lane ? SPR - phi + lane : lane - phi; // tile column
+    const bool odd = jj & 1;
+    const V *zkp = smem + (jj >> 1) * GS + spad(kr0);
+    const V *zmp = smem + (jj >> 1) * GS + spad(L - kr0);
+    for (int it = 0; it < ntile; ++it) {
+      const int64_t task0 = (tile0 + it) * Q;
+      if (load_tile(c, task0)) {
+        if constexpr (TWS)
+          fft_group_tw_m<T, L, E, P, G, M>(v, buf, GS, t, g, row);
+        else
+          fft_group<T, L, E, P, G>(v[0], buf, t, g, p.tw);
+        static_for<0, M>([&](auto mIC) {
+          constexpr int m = decltype(mIC)::value;
+          if (p.dc_mode == 1 && t == 0)
+            v[m][0] = {T(0), T(0)};
+          store_bins<L, E, P>(v[m], buf + m * GS, t);
+          if (t == 0)
+            buf[m * GS + spad_size(L)] = v[m][0];
+        });
+      }
+      __syncthreads();
+
+      // Store.  A thread's bin rows are k = kr0 + ii*RPI with RPI a multiple
+      // of the sector length, so the row's sector phase phi (its columns
+      // col0 - phi + lane, lane < 2Q, are whole sectors) is fixed for the
+      // unit; lanes >= phi write columns col0 + lane - phi of this tile,
+      // lanes < phi write the previous tile's carried column and compute this
+      // tile's trailing column SPR - phi + lane (carried, or written at the
+      // unit's end).
+      const bool first = it == 0;
+      const bool last = it == ntile - 1;
+      const int64_t col0 = 2 * task0;
+      V *rp0 = outc + (int64_t)kr0 * p.o_rs + col0 - phi;
+      const int64_t rstep = (int64_t)RPI * p.o_rs;
+      // per-tile predicates: write this lane's column (this tile's value, or
+      // the carried one), write this tile's trailing column, or carry it
+      const bool wmain = (col0 - phi + lane) < p.S && (!carry_lane || !first);
+      const bool wtrail = carry_lane && last && (col0 + jj) < p.S;
+      const bool wcarry = carry_lane && !last;
+      static_for<0, NIT>([&](auto iIC) {
+        constexpr int ii = decltype(iIC)::value;
+        const int k = kr0 + ii * RPI;
+        if (ii + 1 < NIT || k < FH) {
+          const V zk = zkp[ii * pad_off<RPI>()];
+          const V zm = zmp[-ii * pad_off<RPI>()];
+          // even: A = zk + conj zm; odd: B = -i (zk - conj zm)
+          const T u = odd ? zk.y : zk.x;
+          const T w = odd ? zm.y : zm.x;
+          const T u2 = odd ? zm.x : zk.y;
+          const T w2 = odd ? zk.x : zm.y;
+          const V val = V{u + w, u2 - w2};
+          V *rp = rp0 + ii * rstep;
+          V *cr = carry + k * (SEC - 1) + lane;
+          V sv = val;
+          if (carry_lane)
+            sv = *cr;
+          if (wmain)
+            rp[lane] = sv;
+          if (wtrail)
+            rp[phi + jj] = val;
+          if (wcarry)
+            *cr = val;
+        }
+      });
+      __syncthreads();
+    }
   }
 }
 

@@ -135,7 +135,8 @@ def test_spectrogram(cuda, dtype, mode, nperseg, nfft, detrend):
 
 
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
-@pytest.mark.parametrize("nperseg,noverlap", [(2048, 1536), (512, 0), (1024, 1000)])
+@pytest.mark.parametrize("nperseg,noverlap", [(2048, 1536), (512, 0), (1024, 1000),
+                                              (1024, 512), (8192, 6144), (64, 48)])
 def test_stft(cuda, dtype, nperseg, noverlap):
     x = _sig(40 * nperseg + 1, dtype, 9)
     r = ib.stft(_to_gpu(x, cuda), fs=1e3, nperseg=nperseg, noverlap=noverlap)
@@ -293,3 +294,21 @@ def test_errors_match_reference(cuda):
         ib.spectrogram(x, nperseg=256)
     with pytest.raises(RuntimeError, match="unknown window name 'nope'"):
         ib.welch(x, nperseg=16, window="nope")
+
+
+def test_stft_batched_long_units(cuda):
+    """A batch large enough that each CTA stores several consecutive tiles of
+    a channel (the per-row sector carry between tiles), odd segment count."""
+    import torch
+    C, N, L, H = 24, (1 << 20) + 265, 2048, 512
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    x = torch.randn((C, N), generator=g, device=cuda, dtype=torch.float32)
+    f, t, z = ib.spectral(ib.OP_STFT, x, nperseg=L, noverlap=L - H,
+                          complex_output=True)
+    S = (N - L) // H + 1
+    assert z.shape == (C, L // 2 + 1, S) and S % 2 == 1
+    xs = x.cpu().numpy()
+    for c in (0, 11, C - 1):
+        _, _, zr = so.stft(xs[c], nperseg=L, noverlap=L - H, complex_output=True)
+        assert so.max_rel_err(z[c].cpu().numpy(), zr) <= 1e-5
