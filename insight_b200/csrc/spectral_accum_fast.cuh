@@ -1,0 +1,200 @@
+// spectral_accum_fast.cuh — welch / csd fast path (contiguous channels,
+// nperseg == nfft, no detrend or DC-only detrend).
+//
+// One CTA works on a unit (channel, contiguous range of transforms) with G
+// transform groups of P threads; group g takes the unit's transforms
+// g, g + G, ...  Per transform, as the generic accumulate kernel
+// (spectral_kernels.cuh): welch pairs consecutive segments and accumulates
+// |Z[k]|^2 of the bins each thread owns, csd pairs x_s with y_s and
+// accumulates conj(A[k]) B[k] from Z[k], Z[L-k] staged in shared memory.
+// Differences: the window rows and (TWS) the per-thread Stockham twiddles
+// are in shared memory, overlapping samples of welch's two segments are read
+// once (hop = SH * L/R0), and f32 inputs accumulate in f32 for FL transforms
+// before each f64 update, instead of converting and adding in f64 every
+// transform (FL = 16 terms of f32 rounding, far below the 1e-5 parity bar).
+// At the end of a unit the groups' f64 partials are combined in shared
+// memory and folded into the unit's slot of the scratch array, in a fixed
+// order (no atomics).
+#pragma once
+#include "spectral_kernels.cuh"
+
+namespace ib200 {
+
+template <typename T, int L, int E, int G, int SH, bool TWS, int MODE>
+__global__ void __launch_bounds__(G *(L / E))
+    accum_fast_kernel(const SpecArgs<T> p) {
+  using V = typename V2T<T>::type;
+  using PL = Plan<L, E>;
+  using TT = ThreadTw<T, L, E>;
+  constexpr int P = L / E;
+  constexpr int NT = G * P;
+  constexpr int R0 = PL::radix(0);
+  constexpr int FH = L / 2 + 1;
+  constexpr int NB = (FH + P - 1) / P;        // csd bins per thread
+  constexpr int GS = (spad_size(L) + 1) / 2 * 2;
+  constexpr int WS = E + 16 / (int)sizeof(T);
+  constexpr int NACC = MODE == ACC_PSD ? E : 2 * NB;
+  constexpr int FL = sizeof(T) == 4 ? 16 : 1; // transforms per f32 partial
+  static_assert(SH >= 0 && SH < R0, "overlap shift");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  V *bufs = reinterpret_cast<V *>(smem_raw);               // [G][GS]
+  V *tws = bufs + G * GS;                                   // [P][stride]
+  T *wsm = reinterpret_cast<T *>(tws + (TWS ? P * TT::stride() : 0)); // [P][WS]
+  const int g = threadIdx.x / P;
+  const int t = threadIdx.x - g * P;
+  V *buf = bufs + g * GS;
+
+  for (int i = threadIdx.x; i < P * E; i += NT) {
+    const int tt = i / E, e = i - tt * E;
+    wsm[tt * WS + e] = p.win[in_index<L, E, P>(tt, e)];
+  }
+  if constexpr (TWS)
+    fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+  __syncthreads();
+  const V *row = tws + t * TT::stride();
+
+  T wv[E];
+  static_for<0, E>([&](auto eIC) {
+    constexpr int e = decltype(eIC)::value;
+    wv[e] = wsm[t * WS + e];
+  });
+
+  for (int64_t u = blockIdx.x; u < p.U; u += gridDim.x) {
+    const int64_t c = u / p.nq;
+    const int64_t q = u - c * p.nq;
+    const int64_t task0 = q * p.Qt;
+    const int64_t task1 = min(task0 + p.Qt, p.Tc);
+    const T *xc = p.x + c * p.x_cs + t;
+    const T *yc = p.y + c * p.y_cs + t;
+
+    double acc[NACC];
+    T accf[NACC];
+#pragma unroll
+    for (int i = 0; i < NACC; ++i) {
+      acc[i] = 0.0;
+      accf[i] = T(0);
+    }
+    int nf = 0;
+
+    for (int64_t task = task0 + g; task < task1; task += G) {
+      V vv[1][E];
+      V(&v)[E] = vv[0];
+      if constexpr (MODE == ACC_PSD) {
+        const int64_t s = p.seg0 + 2 * task;
+        const bool hasb = (2 * task + 1) < p.S;
+        const T *xa = xc + s * p.step;
+        T ra[E];
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          ra[e] = __ldg(xa + in_index<L, E, P>(0, e));
+        });
+        if (hasb) {
+          static_for<0, E>([&](auto eIC) {
+            constexpr int e = decltype(eIC)::value;
+            constexpr int r = e % R0;
+            T b;
+            if constexpr (SH > 0 && r + SH < R0)
+              b = ra[e + SH];
+            else
+              b = __ldg(xa + p.step + in_index<L, E, P>(0, e));
+            v[e] = {ra[e] * wv[e], b * wv[e]};
+          });
+        } else {
+          static_for<0, E>([&](auto eIC) {
+            constexpr int e = decltype(eIC)::value;
+            v[e] = {ra[e] * wv[e], T(0)};
+          });
+        }
+      } else {
+        const int64_t s = p.seg0 + task;
+        const T *xa = xc + s * p.step;
+        const T *yb = yc + s * p.step;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          constexpr int n = in_index<L, E, P>(0, e);
+          v[e] = {__ldg(xa + n) * wv[e], __ldg(yb + n) * wv[e]};
+        });
+      }
+      if constexpr (TWS)
+        fft_group_tw_m<T, L, E, P, G, 1>(vv, buf, GS, t, g, row);
+      else
+        fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
+      if (p.dc_mode == 1 && t == 0)
+        v[0] = {T(0), T(0)}; // register 0 of thread 0 holds bin 0
+
+      if constexpr (MODE == ACC_PSD) {
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          accf[e] = fma(v[e].x, v[e].x, fma(v[e].y, v[e].y, accf[e]));
+      } else {
+        store_bins<L, E, P>(v, buf, t);
+        group_sync<G, P>(g);
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+          const int k = t + i * P;
+          if (k < FH) {
+            const V zk = buf[spad(k)];
+            const V zm = buf[spad((L - k) & (L - 1))];
+            // conj(A) B = Im(Z[L-k] Z[k]) / 2 - i (|Z[k]|^2 - |Z[L-k]|^2) / 4
+            accf[2 * i] = fma(T(0.5), fma(zm.x, zk.y, zm.y * zk.x), accf[2 * i]);
+            accf[2 * i + 1] =
+                fma(T(0.25),
+                    fma(zm.x, zm.x, zm.y * zm.y) - fma(zk.x, zk.x, zk.y * zk.y),
+                    accf[2 * i + 1]);
+          }
+        }
+        group_sync<G, P>(g);
+      }
+      if (++nf == FL) {
+#pragma unroll
+        for (int i = 0; i < NACC; ++i) {
+          acc[i] += (double)accf[i];
+          accf[i] = T(0);
+        }
+        nf = 0;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NACC; ++i)
+      acc[i] += (double)accf[i];
+
+    // Combine the groups and fold into the unit's scratch slot.
+    __syncthreads(); // every group is done with its transform buffer
+    if constexpr (MODE == ACC_PSD) {
+      double *sm = reinterpret_cast<double *>(buf);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        sm[out_bin<L, E, P>(t, e)] = acc[e];
+    } else {
+      double2 *sm = reinterpret_cast<double2 *>(buf);
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const int k = t + i * P;
+        if (k < FH)
+          sm[k] = make_double2(acc[2 * i], acc[2 * i + 1]);
+      }
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < FH; k += NT) {
+      if constexpr (MODE == ACC_PSD) {
+        double s = 0.0;
+        for (int gg = 0; gg < G; ++gg) {
+          const double *sm = reinterpret_cast<const double *>(bufs + gg * GS);
+          s += sm[k] + sm[(L - k) & (L - 1)];
+        }
+        p.scratch[u * FH + k] = s;
+      } else {
+        double2 s = make_double2(0.0, 0.0);
+        for (int gg = 0; gg < G; ++gg) {
+          const double2 v2 = reinterpret_cast<const double2 *>(bufs + gg * GS)[k];
+          s.x += v2.x;
+          s.y += v2.y;
+        }
+        reinterpret_cast<double2 *>(p.scratch)[u * FH + k] = s;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+} // namespace ib200

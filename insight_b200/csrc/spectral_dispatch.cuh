@@ -3,6 +3,7 @@
 #pragma once
 #include "launch.h"
 #include "spectral_kernels.cuh"
+#include "spectral_accum_fast.cuh"
 
 #include <algorithm>
 
@@ -292,14 +293,131 @@ cudaError_t run_store(const LaunchDesc &d, int num_sms, cudaStream_t stream,
   return cudaGetLastError();
 }
 
+// welch / csd fast path shape: G transform groups (at most 512 threads, a
+// 128-register budget for the f64 accumulators) and whether the per-thread
+// twiddle rows fit next to the transform buffers.
+struct AccShape {
+  int G;
+  bool tws;
+};
+
+template <typename T, int L> constexpr size_t acc_fast_smem(int G, bool tws) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr int GS = (spad_size(L) + 1) / 2 * 2;
+  size_t b = (size_t)G * GS * 2 * sizeof(T) +
+             (size_t)P * (E + 16 / sizeof(T)) * sizeof(T);
+  if (tws)
+    b += (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T);
+  return b;
+}
+
+template <typename T, int L> constexpr AccShape acc_fast_shape() {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr size_t budget = 200 * 1024;
+  int g = 8;
+  while (g > 1 && g * P > 512)
+    --g;
+  if (P % 32 != 0)
+    g = 1;
+  while (g > 1 && (g & (g - 1)) != 0)
+    --g;
+  if (acc_fast_smem<T, L>(g, true) <= budget)
+    return {g, true};
+  while (g > 1 && acc_fast_smem<T, L>(g, false) > budget)
+    g /= 2;
+  if (acc_fast_smem<T, L>(g, false) <= budget)
+    return {g, false};
+  return {0, false};
+}
+
+template <typename T, int L, int MODE, int SH>
+cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
+                              cudaStream_t stream, int64_t *launches) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr AccShape AS = acc_fast_shape<T, L>();
+  constexpr int G = AS.G;
+  auto kern = accum_fast_kernel<T, L, E, G, SH, AS.tws, MODE>;
+  const size_t smem = acc_fast_smem<T, L>(G, AS.tws);
+  static int blocks_per_sm = -1;
+  if (blocks_per_sm < 0) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+      return e;
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G * P, smem);
+    if (e != cudaSuccess)
+      return e;
+    blocks_per_sm = std::max(nb, 1);
+  }
+  SpecArgs<T> a = make_args<T>(d, scratch);
+  AccSplit sp = acc_split(d, num_sms, blocks_per_sm);
+  a.nq = sp.nq;
+  a.Qt = sp.Qt;
+  a.U = sp.U;
+  kern<<<sp.grid, G * P, smem, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return e;
+  const int64_t n = d.C * d.F;
+  const int threads = 256;
+  spectral_finalize_kernel<MODE><<<(unsigned)((n + threads - 1) / threads),
+                                   threads, 0, stream>>>(
+      a.scratch, d.C, sp.nq, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
+      d.out, d.o_cs, d.out_kind);
+  if (launches)
+    *launches += 2;
+  return cudaGetLastError();
+}
+
+template <typename T, int L, int MODE>
+cudaError_t run_accum_any(const LaunchDesc &d, void *scratch, int num_sms,
+                          cudaStream_t stream, int64_t *launches) {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int R0 = Plan<L, E>::radix(0);
+  if constexpr (acc_fast_shape<T, L>().G > 0) {
+    const bool ok = d.x_ss == 1 && (MODE == ACC_PSD || d.y_ss == 1) &&
+                    d.nperseg == d.nfft && d.dc_mode <= 1;
+    if (ok) {
+      int sh = 0;
+      if (MODE == ACC_PSD) {
+        constexpr int Q = L / R0;
+        if (d.step % Q == 0) {
+          const int64_t v = d.step / Q;
+          if (R0 >= 4 && v == R0 / 4)
+            sh = R0 / 4;
+          else if (R0 >= 2 && v == R0 / 2)
+            sh = R0 / 2;
+        }
+      }
+      if constexpr (MODE == ACC_PSD && R0 >= 4) {
+        if (sh == R0 / 4)
+          return run_accum_fast_sh<T, L, MODE, R0 / 4>(d, scratch, num_sms, stream,
+                                                       launches);
+      }
+      if constexpr (MODE == ACC_PSD && R0 >= 2) {
+        if (sh == R0 / 2)
+          return run_accum_fast_sh<T, L, MODE, R0 / 2>(d, scratch, num_sms, stream,
+                                                       launches);
+      }
+      return run_accum_fast_sh<T, L, MODE, 0>(d, scratch, num_sms, stream,
+                                              launches);
+    }
+  }
+  return run_accum<T, L, MODE>(d, scratch, num_sms, stream, launches);
+}
+
 template <typename T, int L>
 cudaError_t run_len(const LaunchDesc &d, void *scratch, int num_sms,
                     cudaStream_t stream, int64_t *launches) {
   switch (d.kind) {
   case LK_PSD:
-    return run_accum<T, L, ACC_PSD>(d, scratch, num_sms, stream, launches);
+    return run_accum_any<T, L, ACC_PSD>(d, scratch, num_sms, stream, launches);
   case LK_CSD:
-    return run_accum<T, L, ACC_CSD>(d, scratch, num_sms, stream, launches);
+    return run_accum_any<T, L, ACC_CSD>(d, scratch, num_sms, stream, launches);
   default:
     return run_store<T, L>(d, num_sms, stream, launches);
   }
