@@ -223,10 +223,10 @@ def reference_call(w, x, y):
     """One reference call on the sample; returns (fn, kind, cores, note)."""
     from oracle import ref_runner
     cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     L, H = w["L"], w["H"]
     if ref_runner.available():
         kind = "reference"
+        cores = ref_runner.set_threads(cores)
         if w["op"] == "stft":
             xs = x.astype("float32")
             fn = lambda: ref_runner.stft(xs, fs=w["fs"], window=w["window"],

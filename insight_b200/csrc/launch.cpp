@@ -36,7 +36,15 @@ size_t scratch_bytes(const LaunchDesc &d, int num_sms) {
     return 0;
   AccSplit s = acc_split(d, num_sms, 1);
   const size_t per = (d.kind == LK_CSD) ? 16 : 8;
-  return (size_t)s.U * (size_t)(d.nfft / 2 + 1) * per;
+  // unit split (generic kernel) or flat split (fast kernel), whichever needs more
+  const int64_t T_all = d.C * s.Tc;
+  int64_t flat = std::min<int64_t>(T_all, (int64_t)std::max(num_sms, 1) *
+                                              kFlatMaxBlocksPerSm) +
+                 d.C - 1;
+  if (d.max_units > 0)
+    flat = std::min<int64_t>(flat, d.max_units);
+  const int64_t slots = std::max<int64_t>(s.U, flat);
+  return (size_t)slots * (size_t)(d.nfft / 2 + 1) * per;
 }
 
 cudaError_t launch(const LaunchDesc &d, void *scratch, int num_sms,

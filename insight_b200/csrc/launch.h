@@ -45,6 +45,10 @@ struct LaunchDesc {
 };
 
 // Bytes of scratch the launch needs (welch / csd unit partials).
+// Upper bound on resident CTAs per SM used by the flat welch / csd split
+// (its scratch holds grid + channels - 1 partial slots).
+constexpr int kFlatMaxBlocksPerSm = 8;
+
 size_t scratch_bytes(const LaunchDesc &d, int num_sms);
 
 // Enqueue the kernels on `stream`.  scratch must hold scratch_bytes(d).

@@ -1,9 +1,11 @@
 // spectral_accum_fast.cuh — welch / csd fast path (contiguous channels,
 // nperseg == nfft, no detrend or DC-only detrend).
 //
-// One CTA works on a unit (channel, contiguous range of transforms) with G
-// transform groups of P threads; group g takes the unit's transforms
-// g, g + G, ...  Per transform, as the generic accumulate kernel
+// CTA b owns the transforms [b*T/n, (b+1)*T/n) of the flattened
+// (channel, transform) space (T = channels * transforms per channel, n CTAs),
+// so every CTA gets the same work to within one transform.  It runs G
+// transform groups of P threads; within each channel of its range group g
+// takes the transforms g, g + G, ...  Per transform, as the generic accumulate kernel
 // (spectral_kernels.cuh): welch pairs consecutive segments and accumulates
 // |Z[k]|^2 of the bins each thread owns, csd pairs x_s with y_s and
 // accumulates conj(A[k]) B[k] from Z[k], Z[L-k] staged in shared memory.
@@ -12,8 +14,10 @@
 // once (hop = SH * L/R0), and f32 inputs accumulate in f32 for FL transforms
 // before each f64 update, instead of converting and adding in f64 every
 // transform (FL = 16 terms of f32 rounding, far below the 1e-5 parity bar).
-// At the end of a unit the groups' f64 partials are combined in shared
-// memory and folded into the unit's slot of the scratch array, in a fixed
+// At the end of each channel of its range the groups' f64 partials are
+// combined in shared memory and written to the slot b + c of the scratch
+// array (slots are distinct because the ranges are ordered);
+// spectral_finalize_flat_kernel sums the slots of a channel in a fixed
 // order (no atomics).
 #pragma once
 #include "spectral_kernels.cuh"
@@ -59,11 +63,14 @@ __global__ void __launch_bounds__(G *(L / E))
     wv[e] = wsm[t * WS + e];
   });
 
-  for (int64_t u = blockIdx.x; u < p.U; u += gridDim.x) {
-    const int64_t c = u / p.nq;
-    const int64_t q = u - c * p.nq;
-    const int64_t task0 = q * p.Qt;
-    const int64_t task1 = min(task0 + p.Qt, p.Tc);
+  // This CTA's share of the flattened (channel, transform) index space.
+  const int64_t T_all = p.C * p.Tc;
+  const int64_t f0 = flat_start(blockIdx.x, T_all, gridDim.x);
+  const int64_t f1 = flat_start(blockIdx.x + 1, T_all, gridDim.x);
+  for (int64_t c = f0 / p.Tc; f0 < f1 && c < p.C && c * p.Tc < f1; ++c) {
+    const int64_t task0 = max(f0, c * p.Tc) - c * p.Tc;
+    const int64_t task1 = min(f1, (c + 1) * p.Tc) - c * p.Tc;
+    const int64_t u = blockIdx.x + c; // partial-sum slot of (CTA, channel)
     const T *xc = p.x + c * p.x_cs + t;
     const T *yc = p.y + c * p.y_cs + t;
 

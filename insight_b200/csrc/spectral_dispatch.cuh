@@ -176,7 +176,7 @@ cudaError_t run_accum(const LaunchDesc &d, void *scratch, int num_sms,
   const int threads = 256;
   const int64_t blocks = (n + threads - 1) / threads;
   spectral_finalize_kernel<MODE><<<(unsigned)blocks, threads, 0, stream>>>(
-      a.scratch, d.C, sp.nq, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
+      a.scratch, d.C, sp.nq, 0, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
       d.out, d.o_cs, d.out_kind);
   if (launches)
     *launches += 2;
@@ -354,11 +354,18 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
     blocks_per_sm = std::max(nb, 1);
   }
   SpecArgs<T> a = make_args<T>(d, scratch);
-  AccSplit sp = acc_split(d, num_sms, blocks_per_sm);
-  a.nq = sp.nq;
-  a.Qt = sp.Qt;
-  a.U = sp.U;
-  kern<<<sp.grid, G * P, smem, stream>>>(a);
+  // Flat split: one CTA per resident slot, each with the same number of
+  // transforms (to within one); CTA b's partial of channel c is slot b + c.
+  const int64_t T_all = d.C * a.Tc;
+  int64_t grid = std::min<int64_t>(
+      T_all, (int64_t)num_sms * std::min(blocks_per_sm, kFlatMaxBlocksPerSm));
+  if (d.max_units > 0) {
+    if (d.max_units < d.C)
+      return cudaErrorInvalidValue;
+    grid = std::min<int64_t>(grid, d.max_units - d.C + 1);
+  }
+  grid = std::max<int64_t>(grid, 1);
+  kern<<<(unsigned)grid, G * P, smem, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return e;
@@ -366,7 +373,7 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
   const int threads = 256;
   spectral_finalize_kernel<MODE><<<(unsigned)((n + threads - 1) / threads),
                                    threads, 0, stream>>>(
-      a.scratch, d.C, sp.nq, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
+      a.scratch, d.C, grid, T_all, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
       d.out, d.o_cs, d.out_kind);
   if (launches)
     *launches += 2;

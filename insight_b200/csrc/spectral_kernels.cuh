@@ -199,14 +199,30 @@ __global__ void __launch_bounds__(L / E)
   }
 }
 
-// Sum the unit partials of each channel in unit order, scale, mask, store.
+// Flat work split: CTA b of n owns the flattened (channel, transform)
+// indices [flat_start(b), flat_start(b + 1)) of T; flat_owner(j) is the CTA
+// that owns index j.
+__host__ __device__ inline int64_t flat_start(int64_t b, int64_t T, int64_t n) {
+  return b * T / n;
+}
+__host__ __device__ inline int64_t flat_owner(int64_t j, int64_t T, int64_t n) {
+  int64_t b = j * n / T; // flat_start(b) <= j
+  while (b + 1 < n && flat_start(b + 1, T, n) <= j)
+    ++b;
+  return b;
+}
+
+// Sum the partials of each channel in slot order, scale, mask, store.
+// Slots: with flat_T == 0, the nq units of channel c are c*nq .. c*nq+nq-1;
+// with flat_T = C * Tc > 0 (flat split over nq CTAs), CTA b's partial of
+// channel c is slot b + c for the CTAs b whose range meets the channel.
 // Partials hold the one-sided bins k <= L/2 (PSD partials hold A[k] + A[L-k],
 // the pair average is the factor 1/2).  For real inputs the two-sided
 // spectrum is the conjugate mirror: P[L-k] = conj(P[k]).
 template <int MODE>
 __global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
-                                         int64_t C, int64_t nq, int64_t L,
-                                         int64_t F, double avg_scale,
+                                         int64_t C, int64_t nq, int64_t flat_T,
+                                         int64_t L, int64_t F, double avg_scale,
                                          int onesided_mask, void *out,
                                          int64_t o_cs, int out_kind) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -216,15 +232,24 @@ __global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
   const int64_t c = i / F, k = i - c * F;
   const bool mirror = k >= FH;
   const int64_t kk = mirror ? L - k : k;
+  int64_t lo, hi;
+  if (flat_T > 0) {
+    const int64_t Tc = flat_T / C;
+    lo = flat_owner(c * Tc, flat_T, nq) + c;
+    hi = flat_owner((c + 1) * Tc - 1, flat_T, nq) + c + 1;
+  } else {
+    lo = c * nq;
+    hi = lo + nq;
+  }
   double re = 0.0, im = 0.0;
   if (MODE == ACC_PSD) {
-    for (int64_t q = 0; q < nq; ++q)
-      re += scratch[(c * nq + q) * FH + kk];
+    for (int64_t q = lo; q < hi; ++q)
+      re += scratch[q * FH + kk];
     re *= 0.5;
   } else {
     const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
-    for (int64_t q = 0; q < nq; ++q) {
-      const double2 v = s2[(c * nq + q) * FH + kk];
+    for (int64_t q = lo; q < hi; ++q) {
+      const double2 v = s2[q * FH + kk];
       re += v.x;
       im += v.y;
     }

@@ -26,6 +26,8 @@
 #include "insight/ops/creation.h"
 #include "insight/ops/signal/spectral_analysis.h"
 
+#include <omp.h>
+
 #include <cmath>
 #include <complex>
 #include <cstring>
@@ -127,6 +129,14 @@ int64_t copy_out(const ins::Array &a, double *dst, int64_t cap) {
 extern "C" {
 
 const char *ref_last_error(void) { return g_err.c_str(); }
+
+// OpenMP threads of the reference's parallel loops on the calling thread
+// (a launcher such as torchrun may have set OMP_NUM_THREADS=1 already).
+int ref_set_threads(int n) {
+  if (n > 0)
+    omp_set_num_threads(n);
+  return omp_get_max_threads();
+}
 
 int ref_init(const char *backend_dir) {
   try {

@@ -45,10 +45,17 @@ def lib():
                                       ctypes.c_char_p, I, I, I, ctypes.c_char_p,
                                       ctypes.c_int, ctypes.c_char_p, ctypes.c_int, P, P,
                                       P, I, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.ref_set_threads.argtypes = [ctypes.c_int]
+        L.ref_set_threads.restype = ctypes.c_int
         if L.ref_init(REF_DIR.encode()) != 0:
             raise RuntimeError("ref_init: " + L.ref_last_error().decode())
         _lib = L
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """Use n OpenMP threads in the reference's loops; returns the count."""
+    return int(lib().ref_set_threads(int(n)))
 
 
 def _dt(x):
