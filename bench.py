@@ -500,9 +500,15 @@ def main():
                     help="channels per GPU (default: the workload's)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg")
+    ap.add_argument("--samples", type=int, default=0,
+                    help="samples per channel (default: the workload's; a "
+                         "smaller case of the same kernel, for profiling)")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     w["name"] = args.workload
+    if args.samples:
+        w["N"] = args.samples
+        w["desc"] += f" [samples per channel overridden: {args.samples}]"
     if args.impl == "reference":
         return run_reference(args, w)
     return run_ours(args, w)

@@ -379,6 +379,83 @@ __device__ __forceinline__ void fill_thread_twiddles(V *tws, const V *tw,
   }
 }
 
+// Per-thread rows of only the first twiddle W^k of every butterfly of the
+// passes after the first (the powers W^{rk} then follow by binary splitting,
+// as with the global table): the light table for lengths whose full rows do
+// not fit in shared memory.  An odd stride keeps the rows of a warp on
+// distinct banks.
+template <typename T, int L, int E> struct ThreadTw1 {
+  using PL = Plan<L, E>;
+  __host__ __device__ static constexpr int offset(int p) {
+    int o = 0;
+    for (int q = 1; q < p; ++q)
+      o += E / PL::radix(q);
+    return o;
+  }
+  __host__ __device__ static constexpr int total() {
+    return offset(PL::passes());
+  }
+  __host__ __device__ static constexpr int stride() { return total() | 1; }
+};
+
+template <typename T, int L, int E, int P, typename V>
+__device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
+                                               int nthreads) {
+  using PL = Plan<L, E>;
+  using TT = ThreadTw1<T, L, E>;
+  constexpr int NPASS = PL::passes();
+  for (int i = tid; i < P * TT::total(); i += nthreads) {
+    const int tt = i / TT::total();
+    const int slot = i - tt * TT::total();
+    V val = {T(1), T(0)};
+    static_for<1, NPASS>([&](auto pIC) {
+      constexpr int p = decltype(pIC)::value;
+      constexpr int R = PL::radix(p);
+      constexpr int NS = PL::ns(p);
+      if (slot >= TT::offset(p) && slot < TT::offset(p + 1)) {
+        const int b = slot - TT::offset(p);
+        const int k = (tt + b * P) & (NS - 1);
+        val = tw[k * (L / (NS * R))];
+      }
+    });
+    rows[tt * TT::stride() + slot] = val;
+  }
+}
+
+template <typename T, int L, int E, int P, int PASS, typename V>
+__device__ __forceinline__ void pass_compute_w1(V *v, const V *row1) {
+  using PL = Plan<L, E>;
+  using TT = ThreadTw1<T, L, E>;
+  constexpr int R = PL::radix(PASS);
+  constexpr int NS = PL::ns(PASS);
+  constexpr int B = E / R;
+  static_for<0, B>([&](auto bIC) {
+    constexpr int b = decltype(bIC)::value;
+    if constexpr (NS > 1)
+      apply_twiddles<R>(v + b * R, row1[TT::offset(PASS) + b]);
+    dft_reg<T, R>(v + b * R);
+  });
+}
+
+// fft_group with the per-thread first-twiddle rows (row1 = this thread's).
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group_w1(V *v, V *buf, int t, int g,
+                                             const V *row1) {
+  constexpr int NP = Plan<L, E>::passes();
+  static_for<0, NP>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+    pass_compute_w1<T, L, E, P, p>(v, row1);
+    if constexpr (p + 1 < NP) {
+      pass_store<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+  });
+}
+
 // pass_compute with the per-thread twiddle row instead of the recurrence.
 template <typename T, int L, int E, int P, int PASS, typename V>
 __device__ __forceinline__ void pass_compute_tw(V *v, const V *row) {

@@ -24,7 +24,39 @@
 
 namespace ib200 {
 
-template <typename T, int L, int E, int G, int SH, bool TWS, int MODE>
+// 16-byte asynchronous global -> shared copies (cp.async, L2 only), and the
+// wait for all of this thread's outstanding copies.  cp.async.wait_group is a
+// hardware wait on the thread's own copies, not a spin loop.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// n contiguous elements (n * sizeof(T) a multiple of 16, both ends 16-byte
+// aligned) from src to dst, spread over the P threads of a group.
+template <typename T, int P>
+__device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
+                                           int t) {
+  constexpr int PER = 16 / (int)sizeof(T);
+  const int nch = (int)(n / PER);
+  for (int j = t; j < nch; j += P)
+    cp_async16(dst + j * PER, src + j * PER);
+}
+
+// STG: segment samples are staged in shared memory by cp.async one transform
+// ahead (the copy for a group's next transform is in flight during this
+// transform's FFT); requires 16-byte aligned segment starts.  Without STG
+// the samples are loaded straight into registers.
+// TWM: Stockham twiddles from the global table (0), from per-thread rows of
+// the first twiddle of each butterfly (1), or from full per-thread rows (2).
+template <typename T, int L, int E, int G, int SH, int TWM, int MODE, bool STG>
 __global__ void __launch_bounds__(G *(L / E))
     accum_fast_kernel(const SpecArgs<T> p) {
   using V = typename V2T<T>::type;
@@ -42,20 +74,26 @@ __global__ void __launch_bounds__(G *(L / E))
   static_assert(SH >= 0 && SH < R0, "overlap shift");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   V *bufs = reinterpret_cast<V *>(smem_raw);               // [G][GS]
-  V *tws = bufs + G * GS;                                   // [P][stride]
-  T *wsm = reinterpret_cast<T *>(tws + (TWS ? P * TT::stride() : 0)); // [P][WS]
+  T *raws = reinterpret_cast<T *>(bufs + G * GS);          // [G][2L] (STG)
+  V *tws = reinterpret_cast<V *>(raws + (STG ? G * 2 * L : 0)); // [P][stride]
+  constexpr int TWROW = TWM == 2 ? TT::stride()
+                                 : (TWM == 1 ? ThreadTw1<T, L, E>::stride() : 0);
+  T *wsm = reinterpret_cast<T *>(tws + P * TWROW);                // [P][WS]
   const int g = threadIdx.x / P;
   const int t = threadIdx.x - g * P;
   V *buf = bufs + g * GS;
+  T *raw = raws + g * 2 * L;
 
   for (int i = threadIdx.x; i < P * E; i += NT) {
     const int tt = i / E, e = i - tt * E;
     wsm[tt * WS + e] = p.win[in_index<L, E, P>(tt, e)];
   }
-  if constexpr (TWS)
+  if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+  else if constexpr (TWM == 1)
+    fill_thread_w1<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   __syncthreads();
-  const V *row = tws + t * TT::stride();
+  const V *row = tws + t * TWROW;
 
   T wv[E];
   static_for<0, E>([&](auto eIC) {
@@ -83,10 +121,75 @@ __global__ void __launch_bounds__(G *(L / E))
     }
     int nf = 0;
 
+    // STG: welch copies the pair's span [s*step, (s+1)*step + L) when the
+    // segments overlap (b starts at raw + step), else a at raw, b at raw + L;
+    // csd copies x_s to raw and y_s to raw + L.
+    auto issue = [&](int64_t task) {
+      if constexpr (MODE == ACC_PSD) {
+        const T *xa = p.x + c * p.x_cs + (p.seg0 + 2 * task) * p.step;
+        const bool hasb = (2 * task + 1) < p.S;
+        if (hasb && p.step < L) {
+          stage_copy<T, P>(raw, xa, p.step + L, t);
+        } else {
+          stage_copy<T, P>(raw, xa, L, t);
+          if (hasb)
+            stage_copy<T, P>(raw + L, xa + p.step, L, t);
+        }
+      } else {
+        const int64_t off = (p.seg0 + task) * p.step;
+        stage_copy<T, P>(raw, p.x + c * p.x_cs + off, L, t);
+        stage_copy<T, P>(raw + L, p.y + c * p.y_cs + off, L, t);
+      }
+      cp_async_commit();
+    };
+    if constexpr (STG) {
+      if (task0 + g < task1)
+        issue(task0 + g);
+    }
+
     for (int64_t task = task0 + g; task < task1; task += G) {
       V vv[1][E];
       V(&v)[E] = vv[0];
-      if constexpr (MODE == ACC_PSD) {
+      if constexpr (STG) {
+        cp_async_wait_all();
+        group_sync<G, P>(g); // every thread's copies of this transform landed
+        const T *rt = raw + t;
+        if constexpr (MODE == ACC_PSD) {
+          const bool hasb = (2 * task + 1) < p.S;
+          const int64_t boff = p.step < L ? p.step : L;
+          T ra[E];
+          static_for<0, E>([&](auto eIC) {
+            constexpr int e = decltype(eIC)::value;
+            ra[e] = rt[in_index<L, E, P>(0, e)];
+          });
+          if (hasb) {
+            static_for<0, E>([&](auto eIC) {
+              constexpr int e = decltype(eIC)::value;
+              constexpr int r = e % R0;
+              T b;
+              if constexpr (SH > 0 && r + SH < R0)
+                b = ra[e + SH];
+              else
+                b = rt[boff + in_index<L, E, P>(0, e)];
+              v[e] = {ra[e] * wv[e], b * wv[e]};
+            });
+          } else {
+            static_for<0, E>([&](auto eIC) {
+              constexpr int e = decltype(eIC)::value;
+              v[e] = {ra[e] * wv[e], T(0)};
+            });
+          }
+        } else {
+          static_for<0, E>([&](auto eIC) {
+            constexpr int e = decltype(eIC)::value;
+            constexpr int n = in_index<L, E, P>(0, e);
+            v[e] = {rt[n] * wv[e], rt[L + n] * wv[e]};
+          });
+        }
+        group_sync<G, P>(g); // the staging buffer is free again
+        if (task + G < task1)
+          issue(task + G);
+      } else if constexpr (MODE == ACC_PSD) {
         const int64_t s = p.seg0 + 2 * task;
         const bool hasb = (2 * task + 1) < p.S;
         const T *xa = xc + s * p.step;
@@ -122,8 +225,10 @@ __global__ void __launch_bounds__(G *(L / E))
           v[e] = {__ldg(xa + n) * wv[e], __ldg(yb + n) * wv[e]};
         });
       }
-      if constexpr (TWS)
+      if constexpr (TWM == 2)
         fft_group_tw_m<T, L, E, P, G, 1>(vv, buf, GS, t, g, row);
+      else if constexpr (TWM == 1)
+        fft_group_w1<T, L, E, P, G>(v, buf, t, g, row);
       else
         fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
       if (p.dc_mode == 1 && t == 0)

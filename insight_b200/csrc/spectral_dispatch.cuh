@@ -298,24 +298,29 @@ cudaError_t run_store(const LaunchDesc &d, int num_sms, cudaStream_t stream,
 // twiddle rows fit next to the transform buffers.
 struct AccShape {
   int G;
-  bool tws;
+  int twm; // 0 global twiddle table, 1 first-twiddle rows, 2 full rows
 };
 
-template <typename T, int L> constexpr size_t acc_fast_smem(int G, bool tws) {
+template <typename T, int L>
+constexpr size_t acc_fast_smem(int G, int twm, bool stg) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   constexpr int GS = (spad_size(L) + 1) / 2 * 2;
   size_t b = (size_t)G * GS * 2 * sizeof(T) +
              (size_t)P * (E + 16 / sizeof(T)) * sizeof(T);
-  if (tws)
+  if (stg)
+    b += (size_t)G * 2 * L * sizeof(T);
+  if (twm == 2)
     b += (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T);
+  else if (twm == 1)
+    b += (size_t)P * ThreadTw1<T, L, E>::stride() * 2 * sizeof(T);
   return b;
 }
 
-template <typename T, int L> constexpr AccShape acc_fast_shape() {
+template <typename T, int L, bool STG> constexpr AccShape acc_fast_shape() {
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
-  constexpr size_t budget = 200 * 1024;
+  constexpr size_t budget = 220 * 1024;
   int g = 8;
   while (g > 1 && g * P > 512)
     --g;
@@ -323,24 +328,22 @@ template <typename T, int L> constexpr AccShape acc_fast_shape() {
     g = 1;
   while (g > 1 && (g & (g - 1)) != 0)
     --g;
-  if (acc_fast_smem<T, L>(g, true) <= budget)
-    return {g, true};
-  while (g > 1 && acc_fast_smem<T, L>(g, false) > budget)
-    g /= 2;
-  if (acc_fast_smem<T, L>(g, false) <= budget)
-    return {g, false};
-  return {0, false};
+  for (; g >= 1; g /= 2)
+    for (int twm = 2; twm >= 0; --twm)
+      if (acc_fast_smem<T, L>(g, twm, STG) <= budget)
+        return {g, twm};
+  return {0, 0};
 }
 
-template <typename T, int L, int MODE, int SH>
+template <typename T, int L, int MODE, int SH, bool STG>
 cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
                               cudaStream_t stream, int64_t *launches) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
-  constexpr AccShape AS = acc_fast_shape<T, L>();
+  constexpr AccShape AS = acc_fast_shape<T, L, STG>();
   constexpr int G = AS.G;
-  auto kern = accum_fast_kernel<T, L, E, G, SH, AS.tws, MODE>;
-  const size_t smem = acc_fast_smem<T, L>(G, AS.tws);
+  auto kern = accum_fast_kernel<T, L, E, G, SH, AS.twm, MODE, STG>;
+  const size_t smem = acc_fast_smem<T, L>(G, AS.twm, STG);
   static int blocks_per_sm = -1;
   if (blocks_per_sm < 0) {
     cudaError_t e = cudaFuncSetAttribute(
@@ -373,11 +376,25 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
   const int threads = 256;
   spectral_finalize_kernel<MODE><<<(unsigned)((n + threads - 1) / threads),
                                    threads, 0, stream>>>(
-      a.scratch, d.C, grid, T_all, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
-      d.out, d.o_cs, d.out_kind);
+      a.scratch, d.C, grid, T_all, d.nfft, d.F, d.avg_scale,
+      d.onesided_mask ? 1 : 0, d.out, d.o_cs, d.out_kind);
   if (launches)
     *launches += 2;
   return cudaGetLastError();
+}
+
+// Every segment start 16-byte aligned (the cp.async staging condition).
+template <typename T, int MODE>
+bool segments_aligned16(const LaunchDesc &d, int L) {
+  const int64_t sz = sizeof(T);
+  auto al = [](const void *q) {
+    return (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
+  };
+  bool ok = al(d.x) && (d.step * sz) % 16 == 0 && (L * sz) % 16 == 0 &&
+            (d.C == 1 || (d.x_cs * sz) % 16 == 0);
+  if (MODE == ACC_CSD)
+    ok = ok && d.y != nullptr && al(d.y) && (d.C == 1 || (d.y_cs * sz) % 16 == 0);
+  return ok;
 }
 
 template <typename T, int L, int MODE>
@@ -385,9 +402,13 @@ cudaError_t run_accum_any(const LaunchDesc &d, void *scratch, int num_sms,
                           cudaStream_t stream, int64_t *launches) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int R0 = Plan<L, E>::radix(0);
-  if constexpr (acc_fast_shape<T, L>().G > 0) {
+  if constexpr (acc_fast_shape<T, L, false>().G > 0 &&
+                acc_fast_shape<T, L, true>().G > 0) {
     const bool ok = d.x_ss == 1 && (MODE == ACC_PSD || d.y_ss == 1) &&
                     d.nperseg == d.nfft && d.dc_mode <= 1;
+    if (ok && !segments_aligned16<T, MODE>(d, L))
+      return run_accum_fast_sh<T, L, MODE, 0, false>(d, scratch, num_sms, stream,
+                                                     launches);
     if (ok) {
       int sh = 0;
       if (MODE == ACC_PSD) {
@@ -402,16 +423,16 @@ cudaError_t run_accum_any(const LaunchDesc &d, void *scratch, int num_sms,
       }
       if constexpr (MODE == ACC_PSD && R0 >= 4) {
         if (sh == R0 / 4)
-          return run_accum_fast_sh<T, L, MODE, R0 / 4>(d, scratch, num_sms, stream,
-                                                       launches);
+          return run_accum_fast_sh<T, L, MODE, R0 / 4, true>(d, scratch, num_sms,
+                                                             stream, launches);
       }
       if constexpr (MODE == ACC_PSD && R0 >= 2) {
         if (sh == R0 / 2)
-          return run_accum_fast_sh<T, L, MODE, R0 / 2>(d, scratch, num_sms, stream,
-                                                       launches);
+          return run_accum_fast_sh<T, L, MODE, R0 / 2, true>(d, scratch, num_sms,
+                                                             stream, launches);
       }
-      return run_accum_fast_sh<T, L, MODE, 0>(d, scratch, num_sms, stream,
-                                              launches);
+      return run_accum_fast_sh<T, L, MODE, 0, true>(d, scratch, num_sms, stream,
+                                                    launches);
     }
   }
   return run_accum<T, L, MODE>(d, scratch, num_sms, stream, launches);
