@@ -14,6 +14,7 @@ Other workloads (--workload):
               hamming, detrend 'linear' (the reference does not detrend)
   csd         512 f32 channel pairs x 2^21 given as transposed (N, C) views,
               nperseg 2048, 50%, hann, complex64 cross spectra
+  coherence   the csd workload through signal::coherence (F64 Cxy)
   welch_long  one f32 signal of 2^30 samples, nperseg 8192, 50%, blackman,
               sharded by segment range over the ranks with one NCCL
               all-reduce of the F64 partial sums (strong scaling)
@@ -64,6 +65,11 @@ WORKLOADS = {
                     "signal::csd {C} f32 pairs x 2^21 per GPU as transposed "
                     "(samples, channels) views, nperseg 2048, 50%, hann, "
                     "complex64 cross spectra")),
+    "coherence": dict(op="coherence", C=512, N=1 << 21, L=2048, H=1024,
+                      window="hann", dtype="f32", fs=1.0, detrend="constant",
+                      desc=("signal::coherence {C} f32 pairs x 2^21 per GPU as "
+                            "transposed (samples, channels) views, nperseg "
+                            "2048, 50%, hann (one pass over x and y)")),
     "welch_long": dict(op="welch", C=1, N=1 << 30, L=8192, H=4096,
                        window="blackman", dtype="f32", fs=1.0, detrend="constant",
                        desc=("signal::welch one f32 signal of 2^30 samples, "
@@ -149,7 +155,7 @@ def make_inputs(torch, dev, w, rank, C):
         T = N / fs
         x += torch.cos(2 * math.pi * (0.5 * (0.4 * fs / T) * t * t)).float()[None, :]
         return x, None
-    if w["op"] == "csd":
+    if w["op"] in ("csd", "coherence"):
         # x ~ N(0,1); y = 0.7 x[n-17] + 0.3 N(0,1); both as (N, C) views
         x = torch.randn((C, N), generator=g, device=dev, dtype=torch.float32)
         y = 0.7 * torch.roll(x, 17, dims=1) + 0.3 * torch.randn(
@@ -213,7 +219,7 @@ def reference_sample(w):
     import numpy as np
     rng = np.random.default_rng(2000)
     n = {"stft": 1 << 19, "welch": 1 << 20, "welch_f64": 1 << 18,
-         "csd": 1 << 18, "welch_long": 1 << 21}[w["name"]]
+         "csd": 1 << 18, "coherence": 1 << 18, "welch_long": 1 << 21}[w["name"]]
     x = rng.standard_normal(n)
     y = 0.7 * np.roll(x, 17) + 0.3 * rng.standard_normal(n)
     return x, y, n
@@ -236,6 +242,10 @@ def reference_call(w, x, y):
             fn = lambda: ref_runner.csd(x, y, fs=w["fs"], window=w["window"],
                                         nperseg=L, noverlap=L - H)
             note = "reference ins::signal::csd on the F64-promoted pair"
+        elif w["op"] == "coherence":
+            fn = lambda: ref_runner.coherence(x, y, fs=w["fs"], window=w["window"],
+                                              nperseg=L, noverlap=L - H)
+            note = "reference ins::signal::coherence on the F64-promoted pair"
         else:
             fn = lambda: ref_runner.welch(x, fs=w["fs"], window=w["window"],
                                           nperseg=L, noverlap=L - H,
@@ -251,6 +261,9 @@ def reference_call(w, x, y):
         elif w["op"] == "csd":
             fn = lambda: so.csd(x, y, fs=w["fs"], window=w["window"], nperseg=L,
                                 noverlap=L - H)
+        elif w["op"] == "coherence":
+            fn = lambda: so.coherence(x, y, fs=w["fs"], window=w["window"],
+                                      nperseg=L, noverlap=L - H)
         else:
             fn = lambda: so.welch(x, fs=w["fs"], window=w["window"], nperseg=L,
                                   noverlap=L - H)
@@ -269,7 +282,7 @@ def cpu_baseline(w, min_s=10.0):
         el = time.perf_counter() - t0
         if el >= min_s or k >= 100:
             break
-    per = n * (2 if w["op"] == "csd" else 1)
+    per = n * (2 if w["op"] in ("csd", "coherence") else 1)
     gsps = k * per / el / 1e9
     seg = (n - w["L"]) // w["H"] + 1
     desc = (f"{note}, FFT by a substitute DFT for the absent FFTW3; one channel "
@@ -293,7 +306,7 @@ def run_reference(args, w):
     for _ in range(args.steps):
         fn()
     el = time.perf_counter() - t0
-    per = n * (2 if w["op"] == "csd" else 1)
+    per = n * (2 if w["op"] in ("csd", "coherence") else 1)
     v = args.steps * per / el / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "GSamples/s",
@@ -369,8 +382,9 @@ def run_ours(args, w):
         x, y = make_inputs(torch, dev, w, rank, C)
         N = w["N"]
         S = (N - L) // H + 1
-        samples = C * N * (2 if op == "csd" else 1) * world
-        in_bytes = C * N * x.element_size() * (2 if op == "csd" else 1)
+        two = op in ("csd", "coherence")
+        samples = C * N * (2 if two else 1) * world
+        in_bytes = C * N * x.element_size() * (2 if two else 1)
         if op == "stft":
             out = torch.empty((C, F, S), dtype=torch.complex64, device=dev)
             out_bytes = C * F * S * 8
@@ -383,6 +397,13 @@ def run_ours(args, w):
             nfft_work = 2 * C * S
             def call(xin, yin, o):
                 ib.spectral(ib.OP_CSD, xin, yin, axis=0, out=o, complex_output=True,
+                            detrend=w["detrend"], **kw)
+        elif op == "coherence":
+            out = torch.empty((C, F), dtype=torch.float64, device=dev)
+            out_bytes = C * F * 8
+            nfft_work = 2 * C * S
+            def call(xin, yin, o):
+                ib.spectral(ib.OP_COHERENCE, xin, yin, axis=0, out=o,
                             detrend=w["detrend"], **kw)
         else:
             out = torch.empty((C, F), dtype=torch.float64, device=dev)
@@ -418,7 +439,8 @@ def run_ours(args, w):
     # end to end through the C ABI with pinned host buffers
     e2e = None
     if not args.no_e2e and not is_long:
-        xh = x.cpu().pin_memory() if op != "csd" else x.t().contiguous().cpu().pin_memory().t()
+        xh = (x.cpu().pin_memory() if not two
+              else x.t().contiguous().cpu().pin_memory().t())
         yh = y.t().contiguous().cpu().pin_memory().t() if y is not None else None
         oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
         e2e_steps = max(3, min(args.steps, 10))

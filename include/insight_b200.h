@@ -284,6 +284,10 @@ INSIGHT_B200_API C_Status insight_b200_csd_kernel(void **inputs,
                                                   void **outputs);
 INSIGHT_B200_API C_Status insight_b200_spectrogram_kernel(void **inputs,
                                                           void **outputs);
+/* "coherence" (F32 / F64): inputs as "csd" with out F64 [n_freq] or
+ * [C, n_freq]; onesided must be 1 (the reference's coherence is one-sided). */
+INSIGHT_B200_API C_Status insight_b200_coherence_kernel(void **inputs,
+                                                        void **outputs);
 
 /* ------------------------------------------------------------------------ */
 /* 3. Host entry points                                                      */
@@ -326,12 +330,33 @@ INSIGHT_B200_API C_Status insight_b200_stft(const InsightArray *x, double fs,
                                             InsightArray *f, InsightArray *t,
                                             InsightArray *zxx);
 
+/* Replaces ins::signal::coherence (spectral_analysis.h:76-82,
+ * spectral_analysis.cpp:199-221): Cxy = Pxy^2 / max(Pxx Pyy, 1e-30) (0 where
+ * Pxx Pyy <= 1e-30) with Pxx, Pyy from welch and Pxy the real part that the
+ * reference's csd returns, all one-sided with 'density' scaling, as the
+ * reference composes them.  Computed in one pass over x and y.  cxy is F64
+ * [n_freq] or [C, n_freq]. */
+INSIGHT_B200_API C_Status insight_b200_coherence(
+    const InsightArray *x, const InsightArray *y, double fs, const char *window,
+    int64_t nperseg, int64_t noverlap, int64_t nfft, const char *detrend,
+    InsightArray *f, InsightArray *cxy);
+
+/* Replaces ins::signal::periodogram (spectral_analysis.h:66-74,
+ * spectral_analysis.cpp:189-193), which is welch with nperseg 256 and the
+ * default overlap (128); the window defaults to "boxcar" there.  pxx as in
+ * insight_b200_welch. */
+INSIGHT_B200_API C_Status insight_b200_periodogram(
+    const InsightArray *x, double fs, const char *window, int64_t nfft,
+    const char *detrend, int return_onesided, const char *scaling,
+    InsightArray *f, InsightArray *pxx);
+
 /* Operation codes of the native entry point. */
 enum {
   INSIGHT_B200_OP_WELCH = 0,
   INSIGHT_B200_OP_CSD = 1,
   INSIGHT_B200_OP_SPECTROGRAM = 2,
-  INSIGHT_B200_OP_STFT = 3
+  INSIGHT_B200_OP_STFT = 3,
+  INSIGHT_B200_OP_COHERENCE = 4
 };
 
 /* Native description of one spectral call (strings as in the frontend). */

@@ -1,17 +1,20 @@
 """insight_b200 — B200-native spectral estimation backend for Insight.
 
 Hot path: the reference's ``signal::welch``, ``signal::csd``,
-``signal::spectrogram`` and ``signal::stft`` as one fused sm_100a kernel
-family behind Insight's device-plugin C ABI (include/insight_b200.h).
+``signal::spectrogram`` and ``signal::stft`` (and the compositions
+``coherence`` and ``periodogram``) as one fused sm_100a kernel family behind
+Insight's device-plugin C ABI (include/insight_b200.h).
 """
 from . import _abi  # noqa: F401
-from .signal import (SpectralResult, SpectrogramResult, csd, finalize_sums,  # noqa: F401
-                     spectral, spectral_shape, spectrogram, stft, welch)
+from .signal import (SpectralResult, SpectrogramResult, coherence, csd,  # noqa: F401
+                     finalize_sums, periodogram, spectral, spectral_shape,
+                     spectrogram, stft, welch)
 
 OP_WELCH = _abi.OP_WELCH
 OP_CSD = _abi.OP_CSD
 OP_SPECTROGRAM = _abi.OP_SPECTROGRAM
 OP_STFT = _abi.OP_STFT
+OP_COHERENCE = _abi.OP_COHERENCE
 
 
 def library_path() -> str:

@@ -19,7 +19,7 @@ DT_F32, DT_F64, DT_C32, DT_C64 = 9, 10, 11, 12
 DEV_CPU, DEV_GPU = 0, 1
 C_SUCCESS, C_FAILED, C_ERROR = 0, 2, 3
 
-OP_WELCH, OP_CSD, OP_SPECTROGRAM, OP_STFT = 0, 1, 2, 3
+OP_WELCH, OP_CSD, OP_SPECTROGRAM, OP_STFT, OP_COHERENCE = 0, 1, 2, 3, 4
 
 
 class InsightArray(ctypes.Structure):
@@ -108,10 +108,13 @@ EXPORTS = (
     "insight_b200_welch_kernel",
     "insight_b200_csd_kernel",
     "insight_b200_spectrogram_kernel",
+    "insight_b200_coherence_kernel",
     "insight_b200_welch",
     "insight_b200_csd",
     "insight_b200_spectrogram",
     "insight_b200_stft",
+    "insight_b200_coherence",
+    "insight_b200_periodogram",
     "insight_b200_spectral_shape",
     "insight_b200_spectral",
     "insight_b200_finalize_sums",
@@ -136,7 +139,7 @@ def lib() -> ctypes.CDLL:
         L.InitPluginGPU.argtypes = [ctypes.POINTER(CustomRuntimeParams)]
         L.InitPluginGPU.restype = ctypes.c_int
         for n in ("insight_b200_welch_kernel", "insight_b200_csd_kernel",
-                  "insight_b200_spectrogram_kernel"):
+                  "insight_b200_spectrogram_kernel", "insight_b200_coherence_kernel"):
             f = getattr(L, n)
             f.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]
             f.restype = ctypes.c_int
@@ -152,6 +155,12 @@ def lib() -> ctypes.CDLL:
         L.insight_b200_stft.argtypes = [
             PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64,
             ctypes.c_int64, PA, PA, PA]
+        L.insight_b200_coherence.argtypes = [
+            PA, PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64,
+            ctypes.c_int64, ctypes.c_char_p, PA, PA]
+        L.insight_b200_periodogram.argtypes = [
+            PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_char_p,
+            ctypes.c_int, ctypes.c_char_p, PA, PA]
         PD = ctypes.POINTER(SpectralDesc)
         PI64 = ctypes.POINTER(ctypes.c_int64)
         L.insight_b200_spectral_shape.argtypes = [PD, PA, PI64, PI64, PI64]
@@ -166,7 +175,8 @@ def lib() -> ctypes.CDLL:
             ctypes.c_int32, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p]
         L.insight_b200_welch_noalloc.restype = ctypes.c_int
         for n in ("insight_b200_welch", "insight_b200_csd", "insight_b200_spectrogram",
-                  "insight_b200_stft", "insight_b200_spectral_shape",
+                  "insight_b200_stft", "insight_b200_coherence",
+                  "insight_b200_periodogram", "insight_b200_spectral_shape",
                   "insight_b200_spectral", "insight_b200_finalize_sums"):
             getattr(L, n).restype = ctypes.c_int
         _lib = L

@@ -305,14 +305,16 @@ C_Status run(const Call &c) {
   try {
     // welch runs csd(x, x) in the reference (spectral_analysis.cpp:177-183)
     // and stft runs spectrogram (:330-334), so their messages carry those names.
-    const char *op = (c.op == INSIGHT_B200_OP_CSD || c.op == INSIGHT_B200_OP_WELCH)
-                         ? "csd"
-                         : "spectrogram";
-    const bool acc = (c.op == INSIGHT_B200_OP_WELCH || c.op == INSIGHT_B200_OP_CSD);
+    // coherence runs welch(x) first (:204), so its messages are csd's too.
+    const bool two = c.op == INSIGHT_B200_OP_CSD || c.op == INSIGHT_B200_OP_COHERENCE;
+    const bool acc = two || c.op == INSIGHT_B200_OP_WELCH;
+    const char *op = acc ? "csd" : "spectrogram";
+    check(c.op >= INSIGHT_B200_OP_WELCH && c.op <= INSIGHT_B200_OP_COHERENCE,
+          "insight_b200: unknown operation code");
     check(c.nperseg > 0, std::string(op) + ": nperseg must be positive");
     InView xv = view_input(c.x, c.axis, op);
     InView yv = xv;
-    if (c.op == INSIGHT_B200_OP_CSD) {
+    if (two) {
       check(c.y != nullptr, "csd: inputs are undefined");
       yv = view_input(c.y, c.axis, op);
       check(yv.dtype == xv.dtype, "csd: x and y must have the same dtype");
@@ -409,7 +411,7 @@ C_Status run(const Call &c) {
       return buf.p;
     };
     d.x = stage(xv, st.xin);
-    d.y = (c.op == INSIGHT_B200_OP_CSD) ? stage(yv, st.yin) : nullptr;
+    d.y = two ? stage(yv, st.yin) : nullptr;
 
     // Tables.
     if (c.window_values) {
@@ -456,6 +458,12 @@ C_Status run(const Call &c) {
         d.kind = LK_PSD;
         check(out->dtype == INSIGHT_DTYPE_F64, "welch: output must be F64");
         d.out_kind = c.raw_sums ? OUT_RAW_F64_K : OUT_REAL_F64_K;
+      } else if (c.op == INSIGHT_B200_OP_COHERENCE) {
+        d.kind = LK_COH;
+        check(out->dtype == INSIGHT_DTYPE_F64, "coherence: output must be F64");
+        check(!c.raw_sums, "coherence: raw sums are not available");
+        check(onesided, "coherence: the result is one-sided");
+        d.out_kind = OUT_REAL_F64_K;
       } else {
         d.kind = LK_CSD;
         if (c.raw_sums) {
@@ -545,8 +553,7 @@ C_Status run(const Call &c) {
                                  stream),
                  "cudaMemcpyAsync");
     }
-    const bool must_sync = c.sync || !xv.gpu || !direct ||
-                           (c.op == INSIGHT_B200_OP_CSD && !yv.gpu);
+    const bool must_sync = c.sync || !xv.gpu || !direct || (two && !yv.gpu);
     if (must_sync)
       cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     else
@@ -564,7 +571,8 @@ C_Status run(const Call &c) {
 C_Status shape(const Call &c, int64_t *n_channels, int64_t *n_seg,
                int64_t *n_freq) {
   try {
-    const bool acc = (c.op == INSIGHT_B200_OP_WELCH || c.op == INSIGHT_B200_OP_CSD);
+    const bool acc = c.op == INSIGHT_B200_OP_WELCH || c.op == INSIGHT_B200_OP_CSD ||
+                     c.op == INSIGHT_B200_OP_COHERENCE;
     const char *op = acc ? "csd" : "spectrogram";
     check(c.nperseg > 0, std::string(op) + ": nperseg must be positive");
     InView xv = view_input(c.x, c.axis, op);

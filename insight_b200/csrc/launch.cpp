@@ -15,7 +15,7 @@ bool nfft_supported(int64_t nfft) {
 // scratch (F values) stays a small fraction of the unit's input.
 AccSplit acc_split(const LaunchDesc &d, int num_sms, int blocks_per_sm) {
   AccSplit s{};
-  s.Tc = (d.kind == LK_CSD) ? d.S : (d.S + 1) / 2;
+  s.Tc = tasks_per_channel(d);
   const int64_t total = d.C * s.Tc;
   const int64_t target = (int64_t)std::max(num_sms, 1) * 16;
   int64_t q0 = (total + target - 1) / target;
@@ -35,7 +35,7 @@ size_t scratch_bytes(const LaunchDesc &d, int num_sms) {
   if (d.kind == LK_STORE)
     return 0;
   AccSplit s = acc_split(d, num_sms, 1);
-  const size_t per = (d.kind == LK_CSD) ? 16 : 8;
+  const size_t per = d.kind == LK_COH ? 32 : (d.kind == LK_CSD ? 16 : 8);
   // unit split (generic kernel) or flat split (fast kernel), whichever needs more
   const int64_t T_all = d.C * s.Tc;
   int64_t flat = std::min<int64_t>(T_all, (int64_t)std::max(num_sms, 1) *

@@ -7,7 +7,8 @@
 
 namespace ib200 {
 
-enum LaunchKind { LK_PSD = 0, LK_CSD = 1, LK_STORE = 2 };
+// LK_COH: magnitude-squared coherence of x and y (one pass: Sxx, Syy, Sxy).
+enum LaunchKind { LK_PSD = 0, LK_CSD = 1, LK_STORE = 2, LK_COH = 3 };
 
 // What the kernels write.
 enum OutKindK {
@@ -45,6 +46,14 @@ struct LaunchDesc {
 };
 
 // Bytes of scratch the launch needs (welch / csd unit partials).
+// Transforms per channel: segment pairs, except csd / coherence with f64
+// nfft = 8192 (one segment per transform, x_s and y_s packed; packs_xy in
+// spectral_kernels.cuh).
+inline int64_t tasks_per_channel(const LaunchDesc &d) {
+  const bool two = d.kind == LK_CSD || d.kind == LK_COH;
+  return (two && d.f64 && d.nfft >= 8192) ? d.S : (d.S + 1) / 2;
+}
+
 // Upper bound on resident CTAs per SM used by the flat welch / csd split
 // (its scratch holds grid + channels - 1 partial slots).
 constexpr int kFlatMaxBlocksPerSm = 8;

@@ -490,7 +490,7 @@ C_Status accum_kernel(void **in, void **out, int op) {
   ib200::Call c;
   c.op = op;
   c.x = x;
-  c.y = op == INSIGHT_B200_OP_CSD ? y : nullptr;
+  c.y = op == INSIGHT_B200_OP_WELCH ? nullptr : y;
   c.out = o;
   c.window_values = &w;
   c.nperseg = *(int64_t *)in[4];
@@ -519,6 +519,10 @@ C_Status insight_b200_welch_kernel(void **inputs, void **outputs) {
 
 C_Status insight_b200_csd_kernel(void **inputs, void **outputs) {
   return accum_kernel(inputs, outputs, INSIGHT_B200_OP_CSD);
+}
+
+C_Status insight_b200_coherence_kernel(void **inputs, void **outputs) {
+  return accum_kernel(inputs, outputs, INSIGHT_B200_OP_COHERENCE);
 }
 
 C_Status insight_b200_spectrogram_kernel(void **in, void **out) {
@@ -646,6 +650,8 @@ C_Status InitPluginGPU(CustomRuntimeParams *params) {
                               insight_b200_welch_kernel);
       params->register_kernel("csd", INSIGHT_DEVICE_GPU, dt,
                               insight_b200_csd_kernel);
+      params->register_kernel("coherence", INSIGHT_DEVICE_GPU, dt,
+                              insight_b200_coherence_kernel);
       params->register_kernel("spectrogram", INSIGHT_DEVICE_GPU, dt,
                               insight_b200_spectrogram_kernel);
       params->register_kernel("stft", INSIGHT_DEVICE_GPU, dt,
@@ -708,6 +714,40 @@ C_Status insight_b200_csd(const InsightArray *x, const InsightArray *y,
   c.scaling = scaling ? scaling : "density";
   c.default_device = current_device();
   return ib200::run(c);
+}
+
+C_Status insight_b200_coherence(const InsightArray *x, const InsightArray *y,
+                                double fs, const char *window, int64_t nperseg,
+                                int64_t noverlap, int64_t nfft,
+                                const char *detrend, InsightArray *f,
+                                InsightArray *cxy) {
+  ib200::Call c;
+  c.op = INSIGHT_B200_OP_COHERENCE;
+  c.x = x;
+  c.y = y;
+  c.out = cxy;
+  c.f = f;
+  c.fs = fs;
+  c.window = window ? window : "hann";
+  c.nperseg = nperseg;
+  c.noverlap = noverlap;
+  c.nfft = nfft;
+  c.detrend_constant = detrend && std::string(detrend) == "constant";
+  c.onesided = true;
+  c.scaling = "density";
+  c.default_device = current_device();
+  return ib200::run(c);
+}
+
+C_Status insight_b200_periodogram(const InsightArray *x, double fs,
+                                  const char *window, int64_t nfft,
+                                  const char *detrend, int return_onesided,
+                                  const char *scaling, InsightArray *f,
+                                  InsightArray *pxx) {
+  // periodogram = welch(x, fs, window, 256, 0, nfft, ...)
+  // (spectral_analysis.cpp:189-193)
+  return insight_b200_welch(x, fs, window ? window : "boxcar", 256, 0, nfft,
+                            detrend, return_onesided, scaling, f, pxx);
 }
 
 C_Status insight_b200_spectrogram(const InsightArray *x, double fs,

@@ -1,24 +1,33 @@
-// spectral_accum_fast.cuh — welch / csd fast path (contiguous channels,
-// nperseg == nfft, no detrend or DC-only detrend).
+// spectral_accum_fast.cuh — welch / csd / coherence fast path (unit sample
+// stride, nperseg == nfft, no detrend or DC-only detrend).
 //
-// CTA b owns the transforms [b*T/n, (b+1)*T/n) of the flattened
-// (channel, transform) space (T = channels * transforms per channel, n CTAs),
-// so every CTA gets the same work to within one transform.  It runs G
-// transform groups of P threads; within each channel of its range group g
-// takes the transforms g, g + G, ...  Per transform, as the generic accumulate kernel
-// (spectral_kernels.cuh): welch pairs consecutive segments and accumulates
-// |Z[k]|^2 of the bins each thread owns, csd pairs x_s with y_s and
-// accumulates conj(A[k]) B[k] from Z[k], Z[L-k] staged in shared memory.
-// Differences: the window rows and (TWS) the per-thread Stockham twiddles
-// are in shared memory, overlapping samples of welch's two segments are read
-// once (hop = SH * L/R0), and f32 inputs accumulate in f32 for FL transforms
-// before each f64 update, instead of converting and adding in f64 every
-// transform (FL = 16 terms of f32 rounding, far below the 1e-5 parity bar).
+// CTA b owns the tasks [b*T/n, (b+1)*T/n) of the flattened (channel, task)
+// space (T = channels * tasks per channel, n CTAs), so every CTA gets the
+// same work to within one task.  It runs G transform groups of P threads;
+// within each channel of its range group g takes the tasks g, g + G, ...
+// A task is a pair of consecutive segments a = 2 task, b = 2 task + 1,
+// transformed together as Z = FFT(w a + i w b) (two real sequences per
+// complex transform):
+//   welch     accumulates |Z[k]|^2 of the bins each thread owns
+//             (|A|^2 + |B|^2 follow from the k and L-k terms at the end);
+//   csd       transforms the x pair and the y pair, stages both spectra in
+//             shared memory and accumulates conj(Xa) Ya + conj(Xb) Yb from
+//             Zx[k], Zx[L-k], Zy[k], Zy[L-k];
+//   coherence as csd, plus |Xa|^2 + |Xb|^2 and |Ya|^2 + |Yb|^2.
+// Pairing segments of the same signal (rather than x_s with y_s) keeps the
+// unpacking error of each spectrum relative to that signal's own power, so a
+// quiet y next to a loud x (or y = 0) stays exact to rounding.
+// The window rows and the per-thread Stockham twiddles (TWM) are in shared
+// memory; overlapping samples of a and b are read once (hop = SH * L/R0);
+// with STG the next task's samples are staged by cp.async during this task's
+// transforms; welch on f32 inputs accumulates in f32 for FL tasks before each
+// f64 update (FL = 16 terms of f32 rounding, far below the 1e-5 parity bar);
+// csd and coherence, which hold more accumulators, add into f64 directly.
 // At the end of each channel of its range the groups' f64 partials are
 // combined in shared memory and written to the slot b + c of the scratch
 // array (slots are distinct because the ranges are ordered);
-// spectral_finalize_flat_kernel sums the slots of a channel in a fixed
-// order (no atomics).
+// spectral_finalize_kernel sums the slots of a channel in a fixed order
+// (no atomics).
 #pragma once
 #include "spectral_kernels.cuh"
 
@@ -69,20 +78,26 @@ __global__ void __launch_bounds__(G *(L / E))
   constexpr int NB = (FH + P - 1) / P;        // csd bins per thread
   constexpr int GS = (spad_size(L) + 1) / 2 * 2;
   constexpr int WS = E + 16 / (int)sizeof(T);
-  constexpr int NACC = MODE == ACC_PSD ? E : 2 * NB;
+  constexpr int NACC = MODE == ACC_PSD ? E : (MODE == ACC_CSD ? 2 : 3) * NB;
   constexpr int FL = sizeof(T) == 4 ? 16 : 1; // transforms per f32 partial
+  constexpr int NF = MODE == ACC_PSD ? NACC : 1; // f32 partial accumulators
   static_assert(SH >= 0 && SH < R0, "overlap shift");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  V *bufs = reinterpret_cast<V *>(smem_raw);               // [G][GS]
-  T *raws = reinterpret_cast<T *>(bufs + G * GS);          // [G][2L] (STG)
-  V *tws = reinterpret_cast<V *>(raws + (STG ? G * 2 * L : 0)); // [P][stride]
+  // welch: one transform buffer and a 2L staging span per group; csd and
+  // coherence: x and y buffers, x and y staging spans.
+  constexpr int NBUF = MODE == ACC_PSD ? 1 : 2;
+  constexpr int RAWN = NBUF * 2 * L;
+  V *bufs = reinterpret_cast<V *>(smem_raw);               // [G][NBUF][GS]
+  T *raws = reinterpret_cast<T *>(bufs + G * NBUF * GS);   // [G][RAWN] (STG)
+  V *tws = reinterpret_cast<V *>(raws + (STG ? G * RAWN : 0)); // [P][stride]
   constexpr int TWROW = TWM == 2 ? TT::stride()
                                  : (TWM == 1 ? ThreadTw1<T, L, E>::stride() : 0);
   T *wsm = reinterpret_cast<T *>(tws + P * TWROW);                // [P][WS]
   const int g = threadIdx.x / P;
   const int t = threadIdx.x - g * P;
-  V *buf = bufs + g * GS;
-  T *raw = raws + g * 2 * L;
+  V *buf = bufs + g * NBUF * GS;
+  V *buf2 = buf + (NBUF - 1) * GS;
+  T *raw = raws + g * RAWN;
 
   for (int i = threadIdx.x; i < P * E; i += NT) {
     const int tt = i / E, e = i - tt * E;
@@ -95,11 +110,67 @@ __global__ void __launch_bounds__(G *(L / E))
   __syncthreads();
   const V *row = tws + t * TWROW;
 
-  T wv[E];
-  static_for<0, E>([&](auto eIC) {
+  // welch keeps the window values in registers; csd and coherence (more
+  // accumulators) reread them from the shared-memory row per load.
+  constexpr int NW = MODE == ACC_PSD ? E : 1;
+  T wreg[NW];
+  static_for<0, NW>([&](auto eIC) {
     constexpr int e = decltype(eIC)::value;
-    wv[e] = wsm[t * WS + e];
+    wreg[e] = wsm[t * WS + e];
   });
+  const T *wrow = wsm + t * WS;
+
+  // Windowed pair a + i b of the segments 2 task, 2 task + 1 of one signal:
+  // src points at this thread's first sample of a (shared staging or global
+  // memory), b starts boff samples later; with SH > 0 the samples b shares
+  // with a come from a's registers.
+  auto load_v = [&](V(&v)[E], const T *src, int64_t boff, bool hasb) {
+    T wv[E];
+    static_for<0, E>([&](auto eIC) {
+      constexpr int e = decltype(eIC)::value;
+      if constexpr (MODE == ACC_PSD)
+        wv[e] = wreg[e];
+      else
+        wv[e] = wrow[e];
+    });
+    T ra[E];
+    static_for<0, E>([&](auto eIC) {
+      constexpr int e = decltype(eIC)::value;
+      if constexpr (STG)
+        ra[e] = src[in_index<L, E, P>(0, e)];
+      else
+        ra[e] = __ldg(src + in_index<L, E, P>(0, e));
+    });
+    if (hasb) {
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        constexpr int r = e % R0;
+        T b;
+        if constexpr (SH > 0 && r + SH < R0)
+          b = ra[e + SH];
+        else if constexpr (STG)
+          b = src[boff + in_index<L, E, P>(0, e)];
+        else
+          b = __ldg(src + boff + in_index<L, E, P>(0, e));
+        v[e] = {ra[e] * wv[e], b * wv[e]};
+      });
+    } else {
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        v[e] = {ra[e] * wv[e], T(0)};
+      });
+    }
+  };
+  auto fft = [&](V(&v)[E], V *b) {
+    if constexpr (TWM == 2)
+      fft_group_tw_m<T, L, E, P, G, 1>(&v, b, GS, t, g, row);
+    else if constexpr (TWM == 1)
+      fft_group_w1<T, L, E, P, G>(v, b, t, g, row);
+    else
+      fft_group<T, L, E, P, G>(v, b, t, g, p.tw);
+    if (p.dc_mode == 1 && t == 0)
+      v[0] = {T(0), T(0)}; // register 0 of thread 0 holds bin 0
+  };
 
   // This CTA's share of the flattened (channel, transform) index space.
   const int64_t T_all = p.C * p.Tc;
@@ -109,37 +180,37 @@ __global__ void __launch_bounds__(G *(L / E))
     const int64_t task0 = max(f0, c * p.Tc) - c * p.Tc;
     const int64_t task1 = min(f1, (c + 1) * p.Tc) - c * p.Tc;
     const int64_t u = blockIdx.x + c; // partial-sum slot of (CTA, channel)
-    const T *xc = p.x + c * p.x_cs + t;
-    const T *yc = p.y + c * p.y_cs + t;
+    const T *xc = p.x + c * p.x_cs;
+    const T *yc = p.y + c * p.y_cs;
 
     double acc[NACC];
-    T accf[NACC];
+    T accf[NF];
 #pragma unroll
-    for (int i = 0; i < NACC; ++i) {
+    for (int i = 0; i < NACC; ++i)
       acc[i] = 0.0;
+#pragma unroll
+    for (int i = 0; i < NF; ++i)
       accf[i] = T(0);
-    }
     int nf = 0;
 
-    // STG: welch copies the pair's span [s*step, (s+1)*step + L) when the
-    // segments overlap (b starts at raw + step), else a at raw, b at raw + L;
-    // csd copies x_s to raw and y_s to raw + L.
-    auto issue = [&](int64_t task) {
-      if constexpr (MODE == ACC_PSD) {
-        const T *xa = p.x + c * p.x_cs + (p.seg0 + 2 * task) * p.step;
-        const bool hasb = (2 * task + 1) < p.S;
-        if (hasb && p.step < L) {
-          stage_copy<T, P>(raw, xa, p.step + L, t);
-        } else {
-          stage_copy<T, P>(raw, xa, L, t);
-          if (hasb)
-            stage_copy<T, P>(raw + L, xa + p.step, L, t);
-        }
+    // STG: the pair's span [s*step, (s+1)*step + L) when the segments
+    // overlap (b at + step), else a at + 0 and b at + L; x at raw, y at
+    // raw + 2L.
+    auto issue_one = [&](T *dst, const T *src, bool hasb) {
+      if (hasb && p.step < L) {
+        stage_copy<T, P>(dst, src, p.step + L, t);
       } else {
-        const int64_t off = (p.seg0 + task) * p.step;
-        stage_copy<T, P>(raw, p.x + c * p.x_cs + off, L, t);
-        stage_copy<T, P>(raw + L, p.y + c * p.y_cs + off, L, t);
+        stage_copy<T, P>(dst, src, L, t);
+        if (hasb)
+          stage_copy<T, P>(dst + L, src + p.step, L, t);
       }
+    };
+    auto issue = [&](int64_t task) {
+      const int64_t off = (p.seg0 + 2 * task) * p.step;
+      const bool hasb = (2 * task + 1) < p.S;
+      issue_one(raw, xc + off, hasb);
+      if constexpr (MODE != ACC_PSD)
+        issue_one(raw + 2 * L, yc + off, hasb);
       cp_async_commit();
     };
     if constexpr (STG) {
@@ -148,127 +219,83 @@ __global__ void __launch_bounds__(G *(L / E))
     }
 
     for (int64_t task = task0 + g; task < task1; task += G) {
-      V vv[1][E];
-      V(&v)[E] = vv[0];
+      const bool hasb = (2 * task + 1) < p.S;
+      const int64_t off = (p.seg0 + 2 * task) * p.step;
+      const int64_t boff = STG ? ((hasb && p.step < L) ? p.step : L) : p.step;
+      V v[E];
       if constexpr (STG) {
         cp_async_wait_all();
-        group_sync<G, P>(g); // every thread's copies of this transform landed
-        const T *rt = raw + t;
-        if constexpr (MODE == ACC_PSD) {
-          const bool hasb = (2 * task + 1) < p.S;
-          const int64_t boff = p.step < L ? p.step : L;
-          T ra[E];
-          static_for<0, E>([&](auto eIC) {
-            constexpr int e = decltype(eIC)::value;
-            ra[e] = rt[in_index<L, E, P>(0, e)];
-          });
-          if (hasb) {
-            static_for<0, E>([&](auto eIC) {
-              constexpr int e = decltype(eIC)::value;
-              constexpr int r = e % R0;
-              T b;
-              if constexpr (SH > 0 && r + SH < R0)
-                b = ra[e + SH];
-              else
-                b = rt[boff + in_index<L, E, P>(0, e)];
-              v[e] = {ra[e] * wv[e], b * wv[e]};
-            });
-          } else {
-            static_for<0, E>([&](auto eIC) {
-              constexpr int e = decltype(eIC)::value;
-              v[e] = {ra[e] * wv[e], T(0)};
-            });
-          }
-        } else {
-          static_for<0, E>([&](auto eIC) {
-            constexpr int e = decltype(eIC)::value;
-            constexpr int n = in_index<L, E, P>(0, e);
-            v[e] = {rt[n] * wv[e], rt[L + n] * wv[e]};
-          });
-        }
-        group_sync<G, P>(g); // the staging buffer is free again
-        if (task + G < task1)
-          issue(task + G);
-      } else if constexpr (MODE == ACC_PSD) {
-        const int64_t s = p.seg0 + 2 * task;
-        const bool hasb = (2 * task + 1) < p.S;
-        const T *xa = xc + s * p.step;
-        T ra[E];
-        static_for<0, E>([&](auto eIC) {
-          constexpr int e = decltype(eIC)::value;
-          ra[e] = __ldg(xa + in_index<L, E, P>(0, e));
-        });
-        if (hasb) {
-          static_for<0, E>([&](auto eIC) {
-            constexpr int e = decltype(eIC)::value;
-            constexpr int r = e % R0;
-            T b;
-            if constexpr (SH > 0 && r + SH < R0)
-              b = ra[e + SH];
-            else
-              b = __ldg(xa + p.step + in_index<L, E, P>(0, e));
-            v[e] = {ra[e] * wv[e], b * wv[e]};
-          });
-        } else {
-          static_for<0, E>([&](auto eIC) {
-            constexpr int e = decltype(eIC)::value;
-            v[e] = {ra[e] * wv[e], T(0)};
-          });
-        }
-      } else {
-        const int64_t s = p.seg0 + task;
-        const T *xa = xc + s * p.step;
-        const T *yb = yc + s * p.step;
-        static_for<0, E>([&](auto eIC) {
-          constexpr int e = decltype(eIC)::value;
-          constexpr int n = in_index<L, E, P>(0, e);
-          v[e] = {__ldg(xa + n) * wv[e], __ldg(yb + n) * wv[e]};
-        });
+        group_sync<G, P>(g); // every thread's copies of this task landed
       }
-      if constexpr (TWM == 2)
-        fft_group_tw_m<T, L, E, P, G, 1>(vv, buf, GS, t, g, row);
-      else if constexpr (TWM == 1)
-        fft_group_w1<T, L, E, P, G>(v, buf, t, g, row);
-      else
-        fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
-      if (p.dc_mode == 1 && t == 0)
-        v[0] = {T(0), T(0)}; // register 0 of thread 0 holds bin 0
-
+      load_v(v, STG ? raw + t : xc + off + t, boff, hasb);
       if constexpr (MODE == ACC_PSD) {
+        if constexpr (STG) {
+          group_sync<G, P>(g); // the staging span is free again
+          if (task + G < task1)
+            issue(task + G);
+        }
+        fft(v, buf);
 #pragma unroll
         for (int e = 0; e < E; ++e)
           accf[e] = fma(v[e].x, v[e].x, fma(v[e].y, v[e].y, accf[e]));
       } else {
+        fft(v, buf);
         store_bins<L, E, P>(v, buf, t);
+        load_v(v, STG ? raw + 2 * L + t : yc + off + t, boff, hasb);
+        if constexpr (STG) {
+          group_sync<G, P>(g); // the staging spans are free again
+          if (task + G < task1)
+            issue(task + G);
+        }
+        fft(v, buf2);
+        store_bins<L, E, P>(v, buf2, t);
         group_sync<G, P>(g);
+        // Zx = Xa + i Xb, Zy = Ya + i Yb (segments a, b of x and of y):
+        // 2 Xa = Zx[k] + conj Zx[L-k], 2 Xb = -i (Zx[k] - conj Zx[L-k]).
+        // Partials are 4 (conj(Xa) Ya + conj(Xb) Yb) (and 4 |X|^2, 4 |Y|^2).
 #pragma unroll
         for (int i = 0; i < NB; ++i) {
           const int k = t + i * P;
           if (k < FH) {
-            const V zk = buf[spad(k)];
-            const V zm = buf[spad((L - k) & (L - 1))];
-            // conj(A) B = Im(Z[L-k] Z[k]) / 2 - i (|Z[k]|^2 - |Z[L-k]|^2) / 4
-            accf[2 * i] = fma(T(0.5), fma(zm.x, zk.y, zm.y * zk.x), accf[2 * i]);
-            accf[2 * i + 1] =
-                fma(T(0.25),
-                    fma(zm.x, zm.x, zm.y * zm.y) - fma(zk.x, zk.x, zk.y * zk.y),
-                    accf[2 * i + 1]);
+            const int m = (L - k) & (L - 1);
+            const V xk = buf[spad(k)], xm = buf[spad(m)];
+            const V yk = buf2[spad(k)], ym = buf2[spad(m)];
+            const T xar = xk.x + xm.x, xai = xk.y - xm.y;
+            const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
+            const T yar = yk.x + ym.x, yai = yk.y - ym.y;
+            const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
+            const T re = fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
+            if constexpr (MODE == ACC_COH) {
+              acc[3 * i] +=
+                  (double)fma(xar, xar, fma(xai, xai, fma(xbr, xbr, xbi * xbi)));
+              acc[3 * i + 1] +=
+                  (double)fma(yar, yar, fma(yai, yai, fma(ybr, ybr, ybi * ybi)));
+              acc[3 * i + 2] += (double)re;
+            } else {
+              const T im = fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+              acc[2 * i] += (double)re;
+              acc[2 * i + 1] += (double)im;
+            }
           }
         }
         group_sync<G, P>(g);
       }
-      if (++nf == FL) {
+      if constexpr (MODE == ACC_PSD) {
+        if (++nf == FL) {
 #pragma unroll
-        for (int i = 0; i < NACC; ++i) {
-          acc[i] += (double)accf[i];
-          accf[i] = T(0);
+          for (int i = 0; i < NF; ++i) {
+            acc[i] += (double)accf[i];
+            accf[i] = T(0);
+          }
+          nf = 0;
         }
-        nf = 0;
       }
     }
+    if constexpr (MODE == ACC_PSD) {
 #pragma unroll
-    for (int i = 0; i < NACC; ++i)
-      acc[i] += (double)accf[i];
+      for (int i = 0; i < NF; ++i)
+        acc[i] += (double)accf[i];
+    }
 
     // Combine the groups and fold into the unit's scratch slot.
     __syncthreads(); // every group is done with its transform buffer
@@ -277,35 +304,48 @@ __global__ void __launch_bounds__(G *(L / E))
 #pragma unroll
       for (int e = 0; e < E; ++e)
         sm[out_bin<L, E, P>(t, e)] = acc[e];
-    } else {
-      double2 *sm = reinterpret_cast<double2 *>(buf);
-#pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        const int k = t + i * P;
-        if (k < FH)
-          sm[k] = make_double2(acc[2 * i], acc[2 * i + 1]);
-      }
-    }
-    __syncthreads();
-    for (int k = threadIdx.x; k < FH; k += NT) {
-      if constexpr (MODE == ACC_PSD) {
+      __syncthreads();
+      for (int k = threadIdx.x; k < FH; k += NT) {
         double s = 0.0;
         for (int gg = 0; gg < G; ++gg) {
-          const double *sm = reinterpret_cast<const double *>(bufs + gg * GS);
+          const double *sm =
+              reinterpret_cast<const double *>(bufs + gg * NBUF * GS);
           s += sm[k] + sm[(L - k) & (L - 1)];
         }
         p.scratch[u * FH + k] = s;
-      } else {
-        double2 s = make_double2(0.0, 0.0);
-        for (int gg = 0; gg < G; ++gg) {
-          const double2 v2 = reinterpret_cast<const double2 *>(bufs + gg * GS)[k];
-          s.x += v2.x;
-          s.y += v2.y;
-        }
-        reinterpret_cast<double2 *>(p.scratch)[u * FH + k] = s;
       }
+      __syncthreads();
+    } else {
+      // csd: one round of (re, im); coherence: rounds (Sxx, Syy), (Sxy, 0)
+      constexpr int ROUNDS = MODE == ACC_CSD ? 1 : 2;
+      constexpr int W = MODE == ACC_CSD ? 2 : 3;
+      static_for<0, ROUNDS>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        double2 *sm = reinterpret_cast<double2 *>(buf);
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+          const int k = t + i * P;
+          if (k < FH) {
+            if constexpr (r == 0)
+              sm[k] = make_double2(acc[W * i], acc[W * i + 1]);
+            else
+              sm[k] = make_double2(acc[W * i + W - 1], 0.0);
+          }
+        }
+        __syncthreads();
+        for (int k = threadIdx.x; k < FH; k += NT) {
+          double2 s = make_double2(0.0, 0.0);
+          for (int gg = 0; gg < G; ++gg) {
+            const double2 v2 =
+                reinterpret_cast<const double2 *>(bufs + gg * NBUF * GS)[k];
+            s.x += v2.x;
+            s.y += v2.y;
+          }
+          reinterpret_cast<double2 *>(p.scratch)[ROUNDS * (u * FH + k) + r] = s;
+        }
+        __syncthreads();
+      });
     }
-    __syncthreads();
   }
 }
 

@@ -6,6 +6,7 @@
 #include "spectral_accum_fast.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace ib200 {
 
@@ -130,7 +131,7 @@ SpecArgs<T> make_args(const LaunchDesc &d, void *scratch) {
   a.tw = reinterpret_cast<const V *>(d.tw);
   a.dtab = reinterpret_cast<const V *>(d.dtab);
   a.dc_mode = d.dc_mode;
-  a.Tc = (d.kind == LK_CSD) ? d.S : (d.S + 1) / 2;
+  a.Tc = tasks_per_channel(d);
   a.scratch = reinterpret_cast<double *>(scratch);
   a.F = d.F;
   a.out = d.out;
@@ -150,7 +151,8 @@ cudaError_t run_accum(const LaunchDesc &d, void *scratch, int num_sms,
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   auto kern = spectral_accum_kernel<T, L, E, MODE>;
-  const size_t smem = sizeof(V) * spad_size(L);
+  const size_t smem =
+      sizeof(V) * spad_size(L) * (MODE != ACC_PSD && !packs_xy<T, L>() ? 2 : 1);
   static int blocks_per_sm = -1; // per instantiation; same on every B200
   if (blocks_per_sm < 0) {
     cudaError_t e = cudaFuncSetAttribute(
@@ -302,14 +304,15 @@ struct AccShape {
 };
 
 template <typename T, int L>
-constexpr size_t acc_fast_smem(int G, int twm, bool stg) {
+constexpr size_t acc_fast_smem(int G, int twm, bool stg, int mode) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   constexpr int GS = (spad_size(L) + 1) / 2 * 2;
-  size_t b = (size_t)G * GS * 2 * sizeof(T) +
+  const int nbuf = mode == ACC_PSD ? 1 : 2; // csd, coherence: x and y spectra
+  size_t b = (size_t)G * nbuf * GS * 2 * sizeof(T) +
              (size_t)P * (E + 16 / sizeof(T)) * sizeof(T);
   if (stg)
-    b += (size_t)G * 2 * L * sizeof(T);
+    b += (size_t)G * nbuf * 2 * L * sizeof(T);
   if (twm == 2)
     b += (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T);
   else if (twm == 1)
@@ -317,12 +320,17 @@ constexpr size_t acc_fast_smem(int G, int twm, bool stg) {
   return b;
 }
 
-template <typename T, int L, bool STG> constexpr AccShape acc_fast_shape() {
+// MAXT: threads per CTA (coherence keeps three accumulators per bin and uses
+// at most 256 threads, i.e. up to 255 registers each).  csd and coherence
+// are never shaped for f64 L = 8192 (two spectra do not fit; see packs_xy).
+template <typename T, int L, bool STG, int MODE>
+constexpr AccShape acc_fast_shape() {
+  constexpr int MAXT = MODE == ACC_COH ? 256 : 512;
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   constexpr size_t budget = 220 * 1024;
   int g = 8;
-  while (g > 1 && g * P > 512)
+  while (g > 1 && g * P > MAXT)
     --g;
   if (P % 32 != 0)
     g = 1;
@@ -330,7 +338,7 @@ template <typename T, int L, bool STG> constexpr AccShape acc_fast_shape() {
     --g;
   for (; g >= 1; g /= 2)
     for (int twm = 2; twm >= 0; --twm)
-      if (acc_fast_smem<T, L>(g, twm, STG) <= budget)
+      if (acc_fast_smem<T, L>(g, twm, STG, MODE) <= budget)
         return {g, twm};
   return {0, 0};
 }
@@ -340,10 +348,10 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
                               cudaStream_t stream, int64_t *launches) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
-  constexpr AccShape AS = acc_fast_shape<T, L, STG>();
+  constexpr AccShape AS = acc_fast_shape<T, L, STG, MODE>();
   constexpr int G = AS.G;
   auto kern = accum_fast_kernel<T, L, E, G, SH, AS.twm, MODE, STG>;
-  const size_t smem = acc_fast_smem<T, L>(G, AS.twm, STG);
+  const size_t smem = acc_fast_smem<T, L>(G, AS.twm, STG, MODE);
   static int blocks_per_sm = -1;
   if (blocks_per_sm < 0) {
     cudaError_t e = cudaFuncSetAttribute(
@@ -392,7 +400,7 @@ bool segments_aligned16(const LaunchDesc &d, int L) {
   };
   bool ok = al(d.x) && (d.step * sz) % 16 == 0 && (L * sz) % 16 == 0 &&
             (d.C == 1 || (d.x_cs * sz) % 16 == 0);
-  if (MODE == ACC_CSD)
+  if (MODE != ACC_PSD)
     ok = ok && d.y != nullptr && al(d.y) && (d.C == 1 || (d.y_cs * sz) % 16 == 0);
   return ok;
 }
@@ -402,37 +410,43 @@ cudaError_t run_accum_any(const LaunchDesc &d, void *scratch, int num_sms,
                           cudaStream_t stream, int64_t *launches) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int R0 = Plan<L, E>::radix(0);
-  if constexpr (acc_fast_shape<T, L, false>().G > 0 &&
-                acc_fast_shape<T, L, true>().G > 0) {
+  constexpr AccShape S0 = acc_fast_shape<T, L, false, MODE>();
+  constexpr AccShape S1 = acc_fast_shape<T, L, true, MODE>();
+  // staging only where it costs no transform groups
+  constexpr bool STG_OK = S1.G > 0 && S1.G >= S0.G;
+  if constexpr (S0.G > 0 && !(MODE != ACC_PSD && packs_xy<T, L>())) {
     const bool ok = d.x_ss == 1 && (MODE == ACC_PSD || d.y_ss == 1) &&
                     d.nperseg == d.nfft && d.dc_mode <= 1;
-    if (ok && !segments_aligned16<T, MODE>(d, L))
-      return run_accum_fast_sh<T, L, MODE, 0, false>(d, scratch, num_sms, stream,
-                                                     launches);
     if (ok) {
       int sh = 0;
-      if (MODE == ACC_PSD) {
-        constexpr int Q = L / R0;
-        if (d.step % Q == 0) {
-          const int64_t v = d.step / Q;
-          if (R0 >= 4 && v == R0 / 4)
-            sh = R0 / 4;
-          else if (R0 >= 2 && v == R0 / 2)
-            sh = R0 / 2;
-        }
+      constexpr int Q = L / R0;
+      if (d.step % Q == 0) {
+        const int64_t v = d.step / Q;
+        if (R0 >= 4 && v == R0 / 4)
+          sh = R0 / 4;
+        else if (R0 >= 2 && v == R0 / 2)
+          sh = R0 / 2;
       }
-      if constexpr (MODE == ACC_PSD && R0 >= 4) {
+      const bool stg = STG_OK && segments_aligned16<T, MODE>(d, L);
+      auto go = [&](auto shIC, auto stgIC) {
+        return run_accum_fast_sh<T, L, MODE, decltype(shIC)::value,
+                                 decltype(stgIC)::value>(d, scratch, num_sms,
+                                                         stream, launches);
+      };
+      using F = std::integral_constant<bool, false>;
+      using Tr = std::integral_constant<bool, STG_OK>;
+      if constexpr (R0 >= 4) {
         if (sh == R0 / 4)
-          return run_accum_fast_sh<T, L, MODE, R0 / 4, true>(d, scratch, num_sms,
-                                                             stream, launches);
+          return stg ? go(std::integral_constant<int, R0 / 4>{}, Tr{})
+                     : go(std::integral_constant<int, R0 / 4>{}, F{});
       }
-      if constexpr (MODE == ACC_PSD && R0 >= 2) {
+      if constexpr (R0 >= 2) {
         if (sh == R0 / 2)
-          return run_accum_fast_sh<T, L, MODE, R0 / 2, true>(d, scratch, num_sms,
-                                                             stream, launches);
+          return stg ? go(std::integral_constant<int, R0 / 2>{}, Tr{})
+                     : go(std::integral_constant<int, R0 / 2>{}, F{});
       }
-      return run_accum_fast_sh<T, L, MODE, 0, true>(d, scratch, num_sms, stream,
-                                                    launches);
+      return stg ? go(std::integral_constant<int, 0>{}, Tr{})
+                 : go(std::integral_constant<int, 0>{}, F{});
     }
   }
   return run_accum<T, L, MODE>(d, scratch, num_sms, stream, launches);
@@ -446,6 +460,8 @@ cudaError_t run_len(const LaunchDesc &d, void *scratch, int num_sms,
     return run_accum_any<T, L, ACC_PSD>(d, scratch, num_sms, stream, launches);
   case LK_CSD:
     return run_accum_any<T, L, ACC_CSD>(d, scratch, num_sms, stream, launches);
+  case LK_COH:
+    return run_accum_any<T, L, ACC_COH>(d, scratch, num_sms, stream, launches);
   default:
     return run_store<T, L>(d, num_sms, stream, launches);
   }

@@ -27,7 +27,18 @@
 
 namespace ib200 {
 
-enum AccMode { ACC_PSD = 0, ACC_CSD = 1 };
+// csd / coherence pair consecutive segments of one signal per transform and
+// stage the x and y spectra side by side, except where two spectra do not
+// fit in shared memory (f64, L = 8192): there a task is one segment and
+// x_s, y_s share a transform.  Host and device agree through this function.
+template <typename T, int L> __host__ __device__ constexpr bool packs_xy() {
+  return sizeof(T) == 8 && L >= 8192;
+}
+
+// ACC_COH accumulates, per one-sided bin, Sxx = sum |X|^2, Syy = sum |Y|^2
+// and Sxy = sum Re(conj(X) Y) (magnitude-squared coherence).
+enum AccMode { ACC_PSD = 0, ACC_CSD = 1, ACC_COH = 2 };
+
 
 
 template <typename T> struct SpecArgs {
@@ -91,10 +102,36 @@ __global__ void __launch_bounds__(L / E)
   constexpr int P = L / E;
   constexpr int FH = L / 2 + 1;        // one-sided bins kept per unit
   constexpr int NB = (FH + P - 1) / P; // csd bins per thread
+  constexpr int NACC = MODE == ACC_PSD ? E : (MODE == ACC_CSD ? 2 : 3) * NB;
+  // csd / coherence stage the x-pair and y-pair spectra side by side; where
+  // two spectra do not fit in shared memory (f64, L = 8192) a task is one
+  // segment and x_s, y_s share one transform (Z = X + iY) instead.
+  constexpr bool PACKXY = packs_xy<T, L>() && MODE != ACC_PSD;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  V *buf = reinterpret_cast<V *>(smem_raw);
+  V *buf = reinterpret_cast<V *>(smem_raw);   // x pair (welch: the pair)
+  V *buf2 = buf + spad_size(L);               // y pair (csd, coherence)
   __shared__ V zdc;
   const int t = threadIdx.x;
+
+  // Z = FFT(w a + i w b) of segments a = 2 task, b = 2 task + 1 of channel
+  // base xc (stride ss); with dc_mode 2 the windowed means are removed in
+  // the frequency domain afterwards.
+  auto transform = [&](V *v, const T *xc, int64_t ss, int64_t task, V *b) {
+    const int64_t s = p.seg0 + 2 * task;
+    const bool hasb = (2 * task + 1) < p.S;
+    load_pair<T, L, E, P>(v, xc + s * p.step * ss, xc + (s + 1) * p.step * ss,
+                          ss, ss, hasb, p.nperseg, p.win, t);
+    fft_group<T, L, E, P, 1>(v, b, t, 0, p.tw);
+  };
+  // Bin k of a staged pair spectrum after the detrend of dc_mode.
+  auto bin = [&](const V *b, int k, V m) -> V {
+    V z = b[spad(k)];
+    if (p.dc_mode == 1 && k == 0)
+      z = {T(0), T(0)};
+    else if (p.dc_mode == 2)
+      z = vsub(z, vmul(m, p.dtab[k]));
+    return z;
+  };
 
   for (int64_t u = blockIdx.x; u < p.U; u += gridDim.x) {
     const int64_t c = u / p.nq;
@@ -104,27 +141,15 @@ __global__ void __launch_bounds__(L / E)
     const T *xc = p.x + c * p.x_cs;
     const T *yc = p.y + c * p.y_cs;
 
-    double acc[MODE == ACC_PSD ? E : 2 * NB];
+    double acc[NACC];
 #pragma unroll
-    for (int i = 0; i < (MODE == ACC_PSD ? E : 2 * NB); ++i)
+    for (int i = 0; i < NACC; ++i)
       acc[i] = 0.0;
 
     for (int64_t task = task0; task < task1; ++task) {
       V v[E];
-      if constexpr (MODE == ACC_PSD) {
-        const int64_t s = p.seg0 + 2 * task;
-        const bool hasb = (2 * task + 1) < p.S;
-        load_pair<T, L, E, P>(v, xc + s * p.step * p.x_ss,
-                              xc + (s + 1) * p.step * p.x_ss, p.x_ss, p.x_ss,
-                              hasb, p.nperseg, p.win, t);
-      } else {
-        const int64_t s = p.seg0 + task;
-        load_pair<T, L, E, P>(v, xc + s * p.step * p.x_ss,
-                              yc + s * p.step * p.y_ss, p.x_ss, p.y_ss, true,
-                              p.nperseg, p.win, t);
-      }
-      fft_group<T, L, E, P, 1>(v, buf, t, 0, p.tw);
-
+      if constexpr (!PACKXY)
+        transform(v, xc, p.x_ss, task, buf);
       if constexpr (MODE == ACC_PSD) {
         if (p.dc_mode == 1) {
           if (t == 0)
@@ -144,33 +169,76 @@ __global__ void __launch_bounds__(L / E)
 #pragma unroll
         for (int e = 0; e < E; ++e)
           acc[e] += (double)fma(v[e].x, v[e].x, v[e].y * v[e].y);
-      } else {
+      } else if constexpr (PACKXY) {
+        // Z = FFT(w x_s + i w y_s), s = task (tasks are segments here)
+        const int64_t s = p.seg0 + task;
+        load_pair<T, L, E, P>(v, xc + s * p.step * p.x_ss, yc + s * p.step * p.y_ss,
+                              p.x_ss, p.y_ss, true, p.nperseg, p.win, t);
+        fft_group<T, L, E, P, 1>(v, buf, t, 0, p.tw);
         store_bins<L, E, P>(v, buf, t);
         __syncthreads();
-        V m = {T(0), T(0)};
-        if (p.dc_mode == 2) {
-          const V z0 = buf[0];
-          const T inv = T(1) / T(p.nperseg);
-          m = {z0.x * inv, z0.y * inv};
-        }
+        const T inv = T(1) / T(p.nperseg);
+        V mz = {T(0), T(0)};
+        if (p.dc_mode == 2)
+          mz = {buf[0].x * inv, buf[0].y * inv};
+        // 2X = Z[k] + conj Z[L-k], 2Y = -i (Z[k] - conj Z[L-k])
 #pragma unroll
         for (int i = 0; i < NB; ++i) {
           const int k = t + i * P;
           if (k < FH) {
-            V zk = buf[spad(k)];
-            V zm = buf[spad((L - k) & (L - 1))];
-            if (p.dc_mode == 1) {
-              if (k == 0)
-                zk = zm = {T(0), T(0)};
-            } else if (p.dc_mode == 2) {
-              zk = vsub(zk, vmul(m, p.dtab[k]));
-              zm = vsub(zm, vmul(m, p.dtab[(L - k) & (L - 1)]));
+            const int m = (L - k) & (L - 1);
+            const V zk = bin(buf, k, mz), zm = bin(buf, m, mz);
+            const T xr = zk.x + zm.x, xi = zk.y - zm.y;
+            const T yr = zk.y + zm.y, yi = zm.x - zk.x;
+            const T re = fma(xr, yr, xi * yi);
+            if constexpr (MODE == ACC_COH) {
+              acc[3 * i] += (double)fma(xr, xr, xi * xi);
+              acc[3 * i + 1] += (double)fma(yr, yr, yi * yi);
+              acc[3 * i + 2] += (double)re;
+            } else {
+              acc[2 * i] += (double)re;
+              acc[2 * i + 1] += (double)fma(xr, yi, -xi * yr);
             }
-            const T re = T(0.5) * fma(zm.x, zk.y, zm.y * zk.x);
-            const T im = T(0.25) * (fma(zm.x, zm.x, zm.y * zm.y) -
-                                    fma(zk.x, zk.x, zk.y * zk.y));
-            acc[2 * i] += (double)re;
-            acc[2 * i + 1] += (double)im;
+          }
+        }
+        __syncthreads();
+      } else {
+        store_bins<L, E, P>(v, buf, t);
+        transform(v, yc, p.y_ss, task, buf2);
+        store_bins<L, E, P>(v, buf2, t);
+        __syncthreads();
+        const T inv = T(1) / T(p.nperseg);
+        V mx = {T(0), T(0)}, my = {T(0), T(0)};
+        if (p.dc_mode == 2) {
+          mx = {buf[0].x * inv, buf[0].y * inv};
+          my = {buf2[0].x * inv, buf2[0].y * inv};
+        }
+        // partials: 4 (conj(Xa) Ya + conj(Xb) Yb), 4 |X|^2, 4 |Y|^2 (see
+        // accum_fast_kernel)
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+          const int k = t + i * P;
+          if (k < FH) {
+            const int m = (L - k) & (L - 1);
+            const V xk = bin(buf, k, mx), xm = bin(buf, m, mx);
+            const V yk = bin(buf2, k, my), ym = bin(buf2, m, my);
+            const T xar = xk.x + xm.x, xai = xk.y - xm.y;
+            const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
+            const T yar = yk.x + ym.x, yai = yk.y - ym.y;
+            const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
+            const T re = fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
+            if constexpr (MODE == ACC_COH) {
+              acc[3 * i] +=
+                  (double)fma(xar, xar, fma(xai, xai, fma(xbr, xbr, xbi * xbi)));
+              acc[3 * i + 1] +=
+                  (double)fma(yar, yar, fma(yai, yai, fma(ybr, ybr, ybi * ybi)));
+              acc[3 * i + 2] += (double)re;
+            } else {
+              const T im =
+                  fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+              acc[2 * i] += (double)re;
+              acc[2 * i + 1] += (double)im;
+            }
           }
         }
         __syncthreads();
@@ -187,13 +255,24 @@ __global__ void __launch_bounds__(L / E)
       for (int k = t; k < FH; k += P)
         p.scratch[u * FH + k] = sm[k] + sm[(L - k) & (L - 1)];
       __syncthreads();
-    } else {
+    } else if constexpr (MODE == ACC_CSD) {
       double2 *s2 = reinterpret_cast<double2 *>(p.scratch);
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
         const int k = t + i * P;
         if (k < FH)
           s2[u * FH + k] = make_double2(acc[2 * i], acc[2 * i + 1]);
+      }
+    } else {
+      // [slot][bin] of (Sxx, Syy), (Sxy, 0)
+      double2 *s2 = reinterpret_cast<double2 *>(p.scratch);
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const int k = t + i * P;
+        if (k < FH) {
+          s2[2 * (u * FH + k)] = make_double2(acc[3 * i], acc[3 * i + 1]);
+          s2[2 * (u * FH + k) + 1] = make_double2(acc[3 * i + 2], 0.0);
+        }
       }
     }
   }
@@ -242,6 +321,29 @@ __global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
     hi = lo + nq;
   }
   double re = 0.0, im = 0.0;
+  if (MODE == ACC_COH) {
+    // Reference coherence (spectral_analysis.cpp:199-221): Pxx, Pyy from
+    // welch, Pxy = Re(csd) (the reference's csd returns the real part), all
+    // with the same scale and mask; Cxy = Pxy^2 / max(Pxx Pyy, 1e-30), and 0
+    // where Pxx Pyy <= 1e-30.
+    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
+    double sxx = 0.0, syy = 0.0, sxy = 0.0;
+    for (int64_t q = lo; q < hi; ++q) {
+      const double2 a = s2[2 * (q * FH + kk)];
+      sxx += a.x;
+      syy += a.y;
+      sxy += s2[2 * (q * FH + kk) + 1].x;
+    }
+    double f = 0.25 * avg_scale; // partials are 4x the sums
+    if (onesided_mask && k >= 1 && k <= F - 2)
+      f *= 2.0;
+    const double pxx = sxx * f, pyy = syy * f, pxy = sxy * f;
+    const double den = pxx * pyy;
+    const double eps = 1e-30;
+    reinterpret_cast<double *>(out)[c * o_cs + k] =
+        den <= eps ? 0.0 : (pxy * pxy) / (den > eps ? den : eps);
+    return;
+  }
   if (MODE == ACC_PSD) {
     for (int64_t q = lo; q < hi; ++q)
       re += scratch[q * FH + kk];
@@ -253,6 +355,8 @@ __global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
       re += v.x;
       im += v.y;
     }
+    re *= 0.25; // partials are 4 conj(X) Y
+    im *= 0.25;
     if (mirror)
       im = -im;
   }

@@ -22,8 +22,9 @@ import numpy as np
 
 from . import _abi
 
-__all__ = ["SpectralResult", "SpectrogramResult", "welch", "csd", "spectrogram",
-           "stft", "spectral", "spectral_shape", "finalize_sums"]
+__all__ = ["SpectralResult", "SpectrogramResult", "welch", "csd", "coherence",
+           "periodogram", "spectrogram", "stft", "spectral", "spectral_shape",
+           "finalize_sums"]
 
 
 @dataclass
@@ -112,7 +113,7 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
     f32 = str(x.dtype).endswith("float32")
     cdt = "complex64" if f32 else "complex128"
     if out is None:
-        if op in (_abi.OP_WELCH, _abi.OP_CSD):
+        if op in (_abi.OP_WELCH, _abi.OP_CSD, _abi.OP_COHERENCE):
             shape = (C, F) if batched else (F,)
             if raw_sums and op == _abi.OP_CSD:
                 dt = "complex128"
@@ -140,8 +141,8 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
     _abi.check(_abi.lib().insight_b200_spectral(
         ctypes.byref(d), ctypes.byref(xa), _abi.ptr(ya), ctypes.byref(oa),
         _abi.ptr(fa), _abi.ptr(ta), st, 1 if sync else 0),
-        ["welch", "csd", "spectrogram", "stft"][op])
-    if op in (_abi.OP_WELCH, _abi.OP_CSD):
+        ["welch", "csd", "spectrogram", "stft", "coherence"][op])
+    if op in (_abi.OP_WELCH, _abi.OP_CSD, _abi.OP_COHERENCE):
         return fo, out
     return fo, to, out
 
@@ -197,6 +198,39 @@ def welch(x, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
         int(noverlap or 0), int(nfft or 0), detrend.encode(),
         1 if return_onesided else 0, scaling.encode(), ctypes.byref(_abi.as_array(f)),
         ctypes.byref(_abi.as_array(pxx))), "welch")
+    return SpectralResult(f, pxx)
+
+
+def coherence(x, y, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
+              detrend="constant"):
+    """Magnitude-squared coherence (reference coherence: Re(Pxy)^2 / (Pxx Pyy),
+    one pass over x and y)."""
+    xa, ya = _abi.as_array(x), _abi.as_array(y)
+    F = _f_out(x, nperseg, nfft, True)
+    shape = (x.shape[0], F) if x.ndim == 2 else (F,)
+    cxy = _empty_like_place(x, shape, "float64")
+    f = _empty_like_place(x, (F,), "float64")
+    _abi.check(_abi.lib().insight_b200_coherence(
+        ctypes.byref(xa), ctypes.byref(ya), float(fs), window.encode(), int(nperseg),
+        int(noverlap or 0), int(nfft or 0), detrend.encode(),
+        ctypes.byref(_abi.as_array(f)), ctypes.byref(_abi.as_array(cxy))),
+        "coherence")
+    return SpectralResult(f, cxy)
+
+
+def periodogram(x, fs=1.0, window="boxcar", nfft=None, detrend="constant",
+                return_onesided=True, scaling="density"):
+    """Reference periodogram: welch with nperseg 256 and the default overlap."""
+    xa = _abi.as_array(x)
+    F = _f_out(x, 256, nfft, return_onesided)
+    shape = (x.shape[0], F) if x.ndim == 2 else (F,)
+    pxx = _empty_like_place(x, shape, "float64")
+    f = _empty_like_place(x, (F,), "float64")
+    _abi.check(_abi.lib().insight_b200_periodogram(
+        ctypes.byref(xa), float(fs), window.encode(), int(nfft or 0),
+        detrend.encode(), 1 if return_onesided else 0, scaling.encode(),
+        ctypes.byref(_abi.as_array(f)), ctypes.byref(_abi.as_array(pxx))),
+        "periodogram")
     return SpectralResult(f, pxx)
 
 

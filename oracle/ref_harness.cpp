@@ -178,6 +178,29 @@ int ref_csd(const void *x, const void *y, int64_t n, int dtype, double fs,
   }
 }
 
+// Reference coherence(x, y) (mode 1) or periodogram(x) (mode 2; nperseg and
+// noverlap are not arguments of the reference's periodogram).
+int ref_coherence(const void *x, const void *y, int64_t n, int dtype, int mode,
+                  double fs, const char *window, int64_t nperseg,
+                  int64_t noverlap, int64_t nfft, const char *detrend,
+                  int onesided, const char *scaling, double *f_out,
+                  double *p_out, int64_t cap, int64_t *n_freq) {
+  try {
+    ins::Array xa = make_input(x, n, dtype);
+    ins::signal::SpectralResult r =
+        mode == 1 ? ins::signal::coherence(xa, make_input(y, n, dtype), fs, window,
+                                           nperseg, noverlap, nfft, detrend)
+                  : ins::signal::periodogram(xa, fs, window, nfft, detrend,
+                                             onesided != 0, scaling);
+    *n_freq = copy_out(r.f, f_out, cap);
+    copy_out(r.Pxx, p_out, cap);
+    return 0;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
 // Reference spectrogram; S is returned (n_seg, n_freq) row-major (the
 // reference returns a transposed view of an (n_freq, n_seg) buffer).
 int ref_spectrogram(const void *x, int64_t n, int dtype, double fs,

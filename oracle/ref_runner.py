@@ -41,6 +41,10 @@ def lib():
                               ctypes.c_double, ctypes.c_char_p, I, I, I,
                               ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p, P, P, I,
                               ctypes.POINTER(I)]
+        L.ref_coherence.argtypes = [ctypes.c_void_p, ctypes.c_void_p, I, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_double, ctypes.c_char_p, I,
+                                    I, I, ctypes.c_char_p, ctypes.c_int,
+                                    ctypes.c_char_p, P, P, I, ctypes.POINTER(I)]
         L.ref_spectrogram.argtypes = [ctypes.c_void_p, I, ctypes.c_int, ctypes.c_double,
                                       ctypes.c_char_p, I, I, I, ctypes.c_char_p,
                                       ctypes.c_int, ctypes.c_char_p, ctypes.c_int, P, P,
@@ -85,6 +89,42 @@ def csd(x, y=None, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
 
 def welch(x, **kw):
     return csd(x, None, **kw)
+
+
+def _coh(mode, x, y, fs, window, nperseg, noverlap, nfft, detrend, onesided,
+         scaling):
+    L = lib()
+    x = np.ascontiguousarray(x)
+    yp = None
+    if y is not None:
+        y = np.ascontiguousarray(y, dtype=x.dtype)
+        yp = y.ctypes.data
+    cap = (nfft or nperseg) + 2
+    f = np.zeros(cap)
+    p = np.zeros(cap)
+    nf = ctypes.c_int64()
+    P = ctypes.POINTER(ctypes.c_double)
+    rc = L.ref_coherence(x.ctypes.data, yp, len(x), _dt(x), mode, fs,
+                         window.encode(), nperseg, noverlap, nfft, detrend.encode(),
+                         1 if onesided else 0, scaling.encode(), f.ctypes.data_as(P),
+                         p.ctypes.data_as(P), cap, ctypes.byref(nf))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    return f[:nf.value].copy(), p[:nf.value].copy()
+
+
+def coherence(x, y, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
+              detrend="constant"):
+    """Reference coherence: returns (f, Cxy) F64."""
+    return _coh(1, x, y, fs, window, nperseg, noverlap, nfft, detrend, True,
+                "density")
+
+
+def periodogram(x, fs=1.0, window="boxcar", nfft=0, detrend="constant",
+                return_onesided=True, scaling="density"):
+    """Reference periodogram (welch with nperseg 256): returns (f, Pxx) F64."""
+    return _coh(2, x, None, fs, window, 256, 0, nfft, detrend, return_onesided,
+                scaling)
 
 
 def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,

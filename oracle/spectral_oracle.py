@@ -184,6 +184,26 @@ def welch(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
                return_onesided, scaling, win=win)
 
 
+def periodogram(x, fs=1.0, window="boxcar", nfft=0, detrend="constant",
+                return_onesided=True, scaling="density"):
+    """Reference periodogram (:189-193) = welch with nperseg 256, noverlap 0
+    (hence the default 128)."""
+    return welch(x, fs, window, 256, 0, nfft, detrend, return_onesided, scaling)
+
+
+def coherence(x, y, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
+              detrend="constant"):
+    """Reference coherence (:199-221): Pxx, Pyy from welch, Pxy the real part
+    csd returns; Cxy = Pxy^2 / max(Pxx Pyy, 1e-30), 0 where Pxx Pyy <= 1e-30."""
+    f, pxx = welch(x, fs, window, nperseg, noverlap, nfft, detrend)
+    _, pyy = welch(y, fs, window, nperseg, noverlap, nfft, detrend)
+    _, pxy = csd(x, y, fs, window, nperseg, noverlap, nfft, detrend)
+    den = pxx * pyy
+    eps = 1e-30
+    cxy = pxy * pxy / np.maximum(den, eps)
+    return f, np.where(den <= eps, 0.0, cxy)
+
+
 def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
                 detrend="constant", return_onesided=True, mode="psd",
                 complex_output=False, win=None):

@@ -55,6 +55,13 @@ CASES = [
     ("stft_f32", "stft", "f32", 3000, dict(fs=1e3, nperseg=128)),
     ("stft_f64_single_segment", "stft", "f64", 512, dict(nperseg=512)),
     ("stft_f64", "stft", "f64", 4000, dict(nperseg=256, noverlap=192)),
+    ("coherence_f64", "coherence", "f64", 5000, dict(fs=2.0, nperseg=256)),
+    ("coherence_f64_pad_hamming_none", "coherence", "f64", 4000,
+     dict(nperseg=200, nfft=256, window="hamming", detrend="none")),
+    ("coherence_f32_promoted", "coherence", "f32", 8192, dict(nperseg=512)),
+    ("periodogram_f64", "periodogram", "f64", 3000, dict(fs=10.0)),
+    ("periodogram_f64_hann_pad_spectrum", "periodogram", "f64", 2000,
+     dict(window="hann", nfft=512, scaling="spectrum")),
 ]
 
 ABI_PROBE = r"""
@@ -111,11 +118,15 @@ def main(ref_tree: str) -> None:
             # sum, spectral_analysis.cpp:63): record the promoted-F64 result
             f, p = ref_runner.welch(x.astype(np.float64), **kw)
             out[name + "/f"], out[name + "/Pxx"] = f, p
-        elif op == "csd":
+        elif op in ("csd", "coherence"):
             y = (0.7 * np.roll(x.astype(np.float64), 17)
                  + 0.3 * signal(n, "f64", 500 + i)).astype(x.dtype)
             out[name + "/y"] = y
-            f, p = ref_runner.csd(x.astype(np.float64), y.astype(np.float64), **kw)
+            fn = ref_runner.csd if op == "csd" else ref_runner.coherence
+            f, p = fn(x.astype(np.float64), y.astype(np.float64), **kw)
+            out[name + "/f"], out[name + "/Pxx"] = f, p
+        elif op == "periodogram":
+            f, p = ref_runner.periodogram(x.astype(np.float64), **kw)
             out[name + "/f"], out[name + "/Pxx"] = f, p
         else:
             # F32 spectrogram/stft in the reference scatter an F32 column into

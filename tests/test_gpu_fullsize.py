@@ -46,13 +46,15 @@ def test_golden_case_on_gpu(case, golden, cuda):
     x = golden[name + "/x"]
     xg = torch.from_numpy(x).to(cuda)
     tol = 1e-5 if x.dtype == np.float32 else 1e-12
-    if op in ("welch", "csd"):
+    if op in ("welch", "csd", "coherence", "periodogram"):
         if op == "welch":
             r = ib.welch(xg, **kw)
-            p = r.Pxx
+        elif op == "periodogram":
+            r = ib.periodogram(xg, **kw)
         else:
-            r = ib.csd(xg, torch.from_numpy(golden[name + "/y"]).to(cuda), **kw)
-            p = r.Pxx
+            yg = torch.from_numpy(golden[name + "/y"]).to(cuda)
+            r = (ib.csd if op == "csd" else ib.coherence)(xg, yg, **kw)
+        p = r.Pxx
         assert np.array_equal(_np(r.f), golden[name + "/f"])
         assert so.max_rel_err(_np(p), golden[name + "/Pxx"]) <= tol
         return

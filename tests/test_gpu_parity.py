@@ -117,6 +117,102 @@ def test_csd(cuda, dtype, nperseg, nfft, detrend, onesided):
     assert so.max_rel_err(_np(pc), pr) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("gain", [1e-3, 0.0])
+@pytest.mark.parametrize("nperseg,nfft", [(1024, 0), (300, 512)])
+def test_csd_and_coherence_with_a_quiet_or_silent_y(cuda, dtype, gain, nperseg,
+                                                    nfft):
+    """Each spectrum is unpacked from transforms of its own signal, so a y far
+    below x (or all zeros) is exact to rounding relative to y itself."""
+    n = 11 * nperseg + 5
+    x = _sig(n, dtype, 7)
+    y = (gain * (0.7 * np.roll(x.astype(np.float64), 3)
+                 + 0.3 * _sig(n, np.float64, 8))).astype(dtype)
+    kw = dict(nperseg=nperseg, nfft=nfft)
+    xg, yg = _to_gpu(x, cuda), _to_gpu(y, cuda)
+    _, pc = ib.spectral(ib.OP_CSD, xg, yg, complex_output=True, **kw)
+    _, pr = so.csd(x, y, complex_output=True, **kw)
+    if gain == 0.0:
+        assert np.array_equal(_np(pc), np.zeros_like(_np(pc)))
+    else:
+        assert so.max_rel_err(_np(pc), pr) <= TOL[dtype]
+    r = ib.coherence(xg, yg, **kw)
+    _, c = so.coherence(x, y, **kw)
+    if gain == 0.0:
+        assert np.array_equal(_np(r.Pxx), np.zeros_like(c))
+    else:
+        assert so.max_rel_err(_np(r.Pxx), c) <= TOL[dtype]
+
+
+# ------------------------------------------------- coherence/periodogram ----
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("nperseg,nfft,window,detrend", [
+    (64, 0, "hann", "constant"), (512, 0, "hamming", "none"),
+    (2048, 0, "hann", "constant"), (8192, 0, "blackman", "constant"),
+    (300, 1024, "hann", "constant"), (200, 256, "hamming", "none")])
+def test_coherence(cuda, dtype, nperseg, nfft, window, detrend):
+    """Fast path (nfft == nperseg) and generic path (zero padding)."""
+    n = 9 * nperseg + 23
+    x = _sig(n, dtype, 3)
+    y = (0.6 * np.roll(x.astype(np.float64), 9) + 0.4 * _sig(n, np.float64, 4)
+         ).astype(dtype)
+    kw = dict(fs=3.0, window=window, nperseg=nperseg, nfft=nfft, detrend=detrend)
+    r = ib.coherence(_to_gpu(x, cuda), _to_gpu(y, cuda), **kw)
+    f, c = so.coherence(x, y, **kw)
+    assert np.array_equal(_np(r.f), f)
+    assert so.max_rel_err(_np(r.Pxx), c) <= TOL[dtype]
+    assert np.all(_np(r.Pxx) >= 0) and np.all(_np(r.Pxx) <= 1 + 1e-6)
+
+
+@pytest.mark.parametrize("layout", ["transposed_view", "interleaved", "host"])
+def test_coherence_batched(cuda, layout):
+    import torch
+    C, N, L = 5, 30000, 1024
+    rng = np.random.default_rng(21)
+    X = rng.standard_normal((C, N)).astype(np.float32)
+    Y = (0.5 * np.roll(X, 3, axis=1) + 0.5 * rng.standard_normal((C, N))
+         ).astype(np.float32)
+    if layout == "transposed_view":   # (N, C) views, unit sample stride
+        xt, yt = _to_gpu(X, cuda).t(), _to_gpu(Y, cuda).t()
+    elif layout == "interleaved":     # (N, C) contiguous: sample stride C
+        xt, yt = _to_gpu(X.T.copy(), cuda), _to_gpu(Y.T.copy(), cuda)
+    else:                             # host arrays, (C, N)
+        xt, yt = X.T.copy(), Y.T.copy()
+    f, c = ib.spectral(ib.OP_COHERENCE, xt, yt, nperseg=L, axis=0)
+    c = _np(c)
+    assert c.shape == (C, L // 2 + 1)
+    for ch in range(C):
+        _, cr = so.coherence(X[ch], Y[ch], nperseg=L)
+        assert so.max_rel_err(c[ch], cr) <= 1e-5
+    if layout != "host":
+        torch.cuda.synchronize()
+
+
+def test_coherence_of_identical_and_zero_signals(cuda):
+    x = _sig(20000, np.float64, 5)
+    r = ib.coherence(_to_gpu(x, cuda), _to_gpu(x, cuda), nperseg=256)
+    c = _np(r.Pxx)
+    assert c[0] == 0.0            # constant detrend empties the DC bin
+    assert np.allclose(c[1:], 1.0, atol=1e-12)
+    z = np.zeros_like(x)
+    r = ib.coherence(_to_gpu(x, cuda), _to_gpu(z, cuda), nperseg=256)
+    assert np.array_equal(_np(r.Pxx), np.zeros(129))   # Pxx Pyy <= 1e-30 -> 0
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("window,nfft,scaling,onesided", [
+    ("boxcar", 0, "density", True), ("hann", 512, "spectrum", True),
+    ("hamming", 0, "density", False)])
+def test_periodogram(cuda, dtype, window, nfft, scaling, onesided):
+    x = _sig(5000, dtype, 6)
+    kw = dict(fs=7.0, window=window, nfft=nfft, scaling=scaling,
+              return_onesided=onesided)
+    r = ib.periodogram(_to_gpu(x, cuda), **kw)
+    f, p = so.periodogram(x, **kw)
+    assert np.array_equal(_np(r.f), f)
+    assert so.max_rel_err(_np(r.Pxx), p) <= TOL[dtype]
+
+
 # ------------------------------------------------------ spectrogram/stft ----
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
 @pytest.mark.parametrize("mode", ["psd", "complex", "magnitude"])
@@ -256,7 +352,7 @@ def test_plugin_registry_kernels(cuda):
     assert lib.InitPluginGPU(ctypes.byref(params)) == 0
     assert params.device_type == b"b200"
     assert (params.version.major, params.version.minor) == (1, 0)
-    for name in ("welch", "csd", "spectrogram", "stft"):
+    for name in ("welch", "csd", "coherence", "spectrogram", "stft"):
         for dt in (_abi.DT_F32, _abi.DT_F64):
             assert (name, _abi.DEV_GPU, dt) in reg
     assert iface.device_memory_allocate and iface.get_last_error
@@ -284,6 +380,16 @@ def test_plugin_registry_kernels(cuda):
     bad = (ctypes.c_void_p * 3)(ctypes.addressof(oa), ctypes.addressof(xa), None)
     assert fn(bad, outs) == _abi.C_FAILED
     assert "expected" in _abi.last_error()
+    # "coherence" through the registry (same layout as "csd")
+    y = (0.5 * np.roll(x, 7) + 0.5 * _sig(40000, np.float32, 9)).astype(np.float32)
+    ya = _abi.from_torch(_to_gpu(y, cuda))
+    ins = (ctypes.c_void_p * 12)(
+        ctypes.addressof(oa), ctypes.addressof(xa), ctypes.addressof(ya),
+        ctypes.addressof(wa), *[ctypes.addressof(v) for v in vals], None)
+    fn = ctypes.cast(reg[("coherence", _abi.DEV_GPU, _abi.DT_F32)], _abi.KERNEL_FN)
+    assert fn(ins, outs) == 0, _abi.last_error()
+    _, c = so.coherence(x, y, fs=1e4, nperseg=L)
+    assert so.max_rel_err(_np(out), c) <= 1e-5
 
 
 def test_errors_match_reference(cuda):

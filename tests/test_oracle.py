@@ -60,9 +60,13 @@ def golden():
 def test_oracle_matches_reference_golden(case, golden):
     name, op, kw = case["name"], case["op"], dict(case["kwargs"])
     x = golden[name + "/x"]
-    if op in ("welch", "csd"):
+    if op in ("welch", "csd", "coherence", "periodogram"):
         if op == "welch":
             f, p = so.welch(x, **kw)
+        elif op == "periodogram":
+            f, p = so.periodogram(x, **kw)
+        elif op == "coherence":
+            f, p = so.coherence(x, golden[name + "/y"], **kw)
         else:
             f, p = so.csd(x, golden[name + "/y"], **kw)
         assert np.array_equal(f, golden[name + "/f"])
