@@ -257,7 +257,10 @@ INSIGHT_B200_API const char *insight_b200_get_last_error(void);
  *              int64_t *nperseg, int64_t *noverlap (resolved, > 0),
  *              int64_t *nfft (resolved, >= nperseg),
  *              int32_t *detrend   (0 none, 1 constant; 'linear' -> 0 as the
- *                                  reference, spectral_analysis.cpp:79),
+ *                                  reference, spectral_analysis.cpp:79;
+ *                                  2 = least-squares line removal after the
+ *                                  window, an extension with no reference
+ *                                  counterpart),
  *              int32_t *onesided,
  *              double  *scale     (compute_psd_scale, spectral_analysis.cpp:57-67),
  *              int64_t *axis,
@@ -368,7 +371,9 @@ typedef struct InsightB200SpectralDesc {
   int64_t nperseg;          /* 0 -> 256                                     */
   int64_t noverlap;         /* 0 -> reference default for the op            */
   int64_t nfft;             /* 0 -> nperseg                                 */
-  const char *detrend;      /* NULL -> "constant"                           */
+  const char *detrend;      /* NULL -> "constant"; "linear_lsq" removes the */
+                            /* least-squares line after the window (the     */
+                            /* reference's "linear" does not detrend)       */
   int32_t return_onesided;
   const char *scaling;      /* welch/csd; NULL -> "density"                 */
   const char *mode;         /* spectrogram; NULL -> "psd"                   */

@@ -364,7 +364,9 @@ C_Status run(const Call &c) {
     double scale = c.has_scale ? c.scale
                                : ((c.scaling == "density" ? c.fs : 1.0) /
                                   window_sum_sq(w, f64));
-    const int dc_mode = !c.detrend_constant ? 0 : (nfft == c.nperseg ? 1 : 2);
+    const int dc_mode = c.detrend_linear ? 3
+                        : !c.detrend_constant ? 0
+                                              : (nfft == c.nperseg ? 1 : 2);
 
     // Result geometry and output arrays.
     std::vector<double> fvec(F);

@@ -24,6 +24,7 @@ struct Call {
   const std::vector<double> *window_values = nullptr; // registry kernels
   int64_t nperseg = 256, noverlap = 0, nfft = 0;
   bool detrend_constant = true;
+  bool detrend_linear = false; // least-squares line removal (native option)
   bool onesided = true;
   std::string scaling = "density";
   std::string mode = "psd";

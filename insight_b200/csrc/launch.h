@@ -33,7 +33,7 @@ struct LaunchDesc {
   const void *win = nullptr;  // [nfft] window in compute dtype
   const void *tw = nullptr;   // [nfft] twiddles in compute dtype
   const void *dtab = nullptr; // [nfft] detrend correction table
-  int dc_mode = 0;
+  int dc_mode = 0; // 0 none, 1 DC bin, 2 zero-padded mean, 3 least-squares line
   int64_t F = 0;              // bins written
   bool onesided_mask = false;
   // welch / csd result

@@ -497,6 +497,7 @@ C_Status accum_kernel(void **in, void **out, int op) {
   c.noverlap = *(int64_t *)in[5];
   c.nfft = *(int64_t *)in[6];
   c.detrend_constant = *(int32_t *)in[7] == 1;
+  c.detrend_linear = *(int32_t *)in[7] == 2;
   c.onesided = *(int32_t *)in[8] != 0;
   c.has_scale = true;
   c.scale = *(double *)in[9];
@@ -548,6 +549,7 @@ C_Status insight_b200_spectrogram_kernel(void **in, void **out) {
   c.noverlap = *(int64_t *)in[4];
   c.nfft = *(int64_t *)in[5];
   c.detrend_constant = *(int32_t *)in[6] == 1;
+  c.detrend_linear = *(int32_t *)in[6] == 2;
   c.onesided = *(int32_t *)in[7] != 0;
   const int mode = *(int32_t *)in[8];
   c.mode = mode == 0 ? "psd" : mode == 1 ? "complex" : "magnitude";
@@ -808,11 +810,15 @@ static ib200::Call from_desc(const InsightB200SpectralDesc *d) {
   c.nfft = d->nfft;
   const char *detrend = d->detrend ? d->detrend : "constant";
   c.detrend_constant = std::string(detrend) == "constant";
+  // native option: least-squares line removal ('linear' stays the
+  // reference's no-op)
+  c.detrend_linear = std::string(detrend) == "linear_lsq";
   c.onesided = d->return_onesided != 0;
   c.scaling = d->scaling ? d->scaling : "density";
   c.mode = d->mode ? d->mode : "psd";
   if (d->op == INSIGHT_B200_OP_STFT) {
     c.detrend_constant = false;
+    c.detrend_linear = false;
     c.onesided = true;
     c.mode = "complex";
   }

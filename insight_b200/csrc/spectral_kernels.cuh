@@ -54,7 +54,8 @@ template <typename T> struct SpecArgs {
   const T *win;        // [nfft], window in T, zero past nperseg
   const V *tw;         // [nfft], W_nfft^m
   const V *dtab;       // [nfft], D[k] (dc_mode 2 only)
-  int dc_mode;         // 0 none, 1 DC bin := 0, 2 zero-padded correction
+  int dc_mode;         // 0 none, 1 DC bin := 0, 2 zero-padded correction,
+                       // 3 least-squares line removal (native 'linear_lsq')
   int64_t Tc;          // transforms per channel
   // accumulate kernels
   int64_t nq;          // work units per channel
@@ -92,6 +93,70 @@ __device__ __forceinline__ void load_pair(typename V2T<T>::type *v,
   });
 }
 
+// Least-squares line removal (detrend after the window, as the constant
+// detrend of the reference frontend, spectral_analysis.cpp:75-82) from both
+// sequences of a packed pair (re = a, im = b) held in pass-0 order; samples
+// at n >= M are zero padding and stay zero.  This is the native 'linear_lsq'
+// option: the reference's 'linear' does not detrend at all.  Sums are
+// reduced in f64 over the group: xor shuffles within a warp (or within the
+// group's lanes when P < 32), then red[(P/32) * 4] per group in shared memory.
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void detrend_linear(V *v, int t, int g, int64_t M,
+                                               double *red) {
+  double s0a = 0.0, s1a = 0.0, s0b = 0.0, s1b = 0.0;
+  static_for<0, E>([&](auto eIC) {
+    constexpr int e = decltype(eIC)::value;
+    const double n = (double)in_index<L, E, P>(t, e);
+    s0a += (double)v[e].x;
+    s1a = fma(n, (double)v[e].x, s1a);
+    s0b += (double)v[e].y;
+    s1b = fma(n, (double)v[e].y, s1b);
+  });
+  constexpr int W = P < 32 ? P : 32;
+  const unsigned lane = threadIdx.x & 31u;
+  const unsigned mask =
+      W == 32 ? 0xffffffffu : (((1u << W) - 1u) << (lane & ~(unsigned)(W - 1)));
+#pragma unroll
+  for (int off = W / 2; off > 0; off >>= 1) {
+    s0a += __shfl_xor_sync(mask, s0a, off);
+    s1a += __shfl_xor_sync(mask, s1a, off);
+    s0b += __shfl_xor_sync(mask, s0b, off);
+    s1b += __shfl_xor_sync(mask, s1b, off);
+  }
+  if constexpr (P > 32) {
+    double *r = red + g * (P / 32) * 4;
+    if ((t & 31) == 0) {
+      const int w = t / 32;
+      r[4 * w] = s0a;
+      r[4 * w + 1] = s1a;
+      r[4 * w + 2] = s0b;
+      r[4 * w + 3] = s1b;
+    }
+    group_sync<G, P>(g);
+    s0a = s1a = s0b = s1b = 0.0;
+    for (int w = 0; w < P / 32; ++w) {
+      s0a += r[4 * w];
+      s1a += r[4 * w + 1];
+      s0b += r[4 * w + 2];
+      s1b += r[4 * w + 3];
+    }
+    group_sync<G, P>(g); // red is free for the next transform
+  }
+  const double Md = (double)M, nb = 0.5 * (Md - 1.0);
+  const double snn = Md * (Md * Md - 1.0) / 12.0; // sum (n - nb)^2
+  const double ba = snn > 0.0 ? (s1a - nb * s0a) / snn : 0.0;
+  const double bb = snn > 0.0 ? (s1b - nb * s0b) / snn : 0.0;
+  const double aa = s0a / Md - ba * nb, ab = s0b / Md - bb * nb;
+  static_for<0, E>([&](auto eIC) {
+    constexpr int e = decltype(eIC)::value;
+    const int n = in_index<L, E, P>(t, e);
+    if (n < M) {
+      v[e].x -= (T)fma(ba, (double)n, aa);
+      v[e].y -= (T)fma(bb, (double)n, ab);
+    }
+  });
+}
+
 // ---------------------------------------------------------------------------
 // welch / csd: accumulate per work unit, one transform group per CTA.
 // ---------------------------------------------------------------------------
@@ -111,22 +176,28 @@ __global__ void __launch_bounds__(L / E)
   V *buf = reinterpret_cast<V *>(smem_raw);   // x pair (welch: the pair)
   V *buf2 = buf + spad_size(L);               // y pair (csd, coherence)
   __shared__ V zdc;
+  __shared__ double red[P > 32 ? (P / 32) * 4 : 1];
   const int t = threadIdx.x;
 
   // Z = FFT(w a + i w b) of segments a = 2 task, b = 2 task + 1 of channel
   // base xc (stride ss); with dc_mode 2 the windowed means are removed in
-  // the frequency domain afterwards.
+  // the frequency domain afterwards, with dc_mode 3 the least-squares lines
+  // before the transform.
   auto transform = [&](V *v, const T *xc, int64_t ss, int64_t task, V *b) {
     const int64_t s = p.seg0 + 2 * task;
     const bool hasb = (2 * task + 1) < p.S;
     load_pair<T, L, E, P>(v, xc + s * p.step * ss, xc + (s + 1) * p.step * ss,
                           ss, ss, hasb, p.nperseg, p.win, t);
+    if (p.dc_mode == 3)
+      detrend_linear<T, L, E, P, 1>(v, t, 0, p.nperseg, red);
     fft_group<T, L, E, P, 1>(v, b, t, 0, p.tw);
   };
   // Bin k of a staged pair spectrum after the detrend of dc_mode.
   auto bin = [&](const V *b, int k, V m) -> V {
     V z = b[spad(k)];
-    if (p.dc_mode == 1 && k == 0)
+    // constant and least-squares detrends leave a residual of zero sum: the
+    // DC bin is exactly zero
+    if ((p.dc_mode == 1 || p.dc_mode == 3) && k == 0)
       z = {T(0), T(0)};
     else if (p.dc_mode == 2)
       z = vsub(z, vmul(m, p.dtab[k]));
@@ -151,7 +222,7 @@ __global__ void __launch_bounds__(L / E)
       if constexpr (!PACKXY)
         transform(v, xc, p.x_ss, task, buf);
       if constexpr (MODE == ACC_PSD) {
-        if (p.dc_mode == 1) {
+        if (p.dc_mode == 1 || p.dc_mode == 3) {
           if (t == 0)
             v[0] = {T(0), T(0)}; // out_bin(0, 0) == 0
         } else if (p.dc_mode == 2) {
@@ -174,6 +245,8 @@ __global__ void __launch_bounds__(L / E)
         const int64_t s = p.seg0 + task;
         load_pair<T, L, E, P>(v, xc + s * p.step * p.x_ss, yc + s * p.step * p.y_ss,
                               p.x_ss, p.y_ss, true, p.nperseg, p.win, t);
+        if (p.dc_mode == 3)
+          detrend_linear<T, L, E, P, 1>(v, t, 0, p.nperseg, red);
         fft_group<T, L, E, P, 1>(v, buf, t, 0, p.tw);
         store_bins<L, E, P>(v, buf, t);
         __syncthreads();
@@ -401,6 +474,7 @@ __global__ void __launch_bounds__(G *(L / E))
   const int g = threadIdx.x / P;
   const int t = threadIdx.x - g * P;
   V *buf = smem + g * GS;
+  __shared__ double red[P > 32 ? G * (P / 32) * 4 : 1];
   const int64_t tpc = (p.Tc + G - 1) / G; // tiles per channel
   const int64_t ntiles = p.C * tpc;
   const T inv_nps = T(1) / T(p.nperseg);
@@ -417,6 +491,8 @@ __global__ void __launch_bounds__(G *(L / E))
       load_pair<T, L, E, P>(v, xc + s * p.step * p.x_ss,
                             xc + (s + 1) * p.step * p.x_ss, p.x_ss, p.x_ss,
                             hasb, p.nperseg, p.win, t);
+      if (p.dc_mode == 3)
+        detrend_linear<T, L, E, P, G>(v, t, g, p.nperseg, red);
       fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
       store_bins<L, E, P>(v, buf, t);
     }
@@ -432,7 +508,7 @@ __global__ void __launch_bounds__(G *(L / E))
       const V *bg = smem + gg * GS;
       V zk = bg[spad(k)];
       V zm = bg[spad((L - k) & (L - 1))];
-      if (p.dc_mode == 1) {
+      if (p.dc_mode == 1 || p.dc_mode == 3) {
         if (k == 0)
           zk = zm = {T(0), T(0)};
       } else if (p.dc_mode == 2) {

@@ -124,7 +124,24 @@ def _transform(x, win, nperseg, step, n_seg, nfft, detrend):
     xw = seg * win[None, :]                                    # :75-76
     if detrend == "constant":                                  # :79-82
         xw = xw - xw.mean(axis=1, keepdims=True)
+    elif detrend == "linear_lsq":
+        # the backend's native option (no reference counterpart: the
+        # reference's 'linear' does not detrend): remove each windowed
+        # segment's least-squares line, as scipy.signal.detrend(type='linear')
+        xw = xw - lsq_line(xw)
     return np.fft.fft(xw, n=nfft, axis=1)                      # :90-91 (pads)
+
+
+def lsq_line(z):
+    """Least-squares line a + b n of each row of z (n = 0 .. M-1)."""
+    M = z.shape[1]
+    n = np.arange(M, dtype=np.float64)
+    nb = (M - 1) / 2.0
+    snn = np.sum((n - nb) ** 2)
+    b = ((z * (n - nb)[None, :]).sum(axis=1) / snn if snn > 0
+         else np.zeros(z.shape[0]))
+    a = z.mean(axis=1) - b * nb
+    return a[:, None] + b[:, None] * n[None, :]
 
 
 def psd_scale(win, fs, scaling):

@@ -144,6 +144,44 @@ def test_csd_and_coherence_with_a_quiet_or_silent_y(cuda, dtype, gain, nperseg,
         assert so.max_rel_err(_np(r.Pxx), c) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("op,nperseg,nfft", [
+    ("welch", 256, 0), ("welch", 200, 512), ("welch", 4096, 0), ("welch", 16, 0),
+    ("csd", 1024, 0), ("coherence", 512, 0), ("stft", 2048, 0),
+    ("spectrogram", 300, 1024)])
+def test_linear_lsq_detrend(cuda, dtype, op, nperseg, nfft):
+    """Native 'linear_lsq' detrend (no reference counterpart) against the
+    oracle's least-squares restatement (pinned to scipy)."""
+    n = 7 * nperseg + 31
+    t = np.arange(n)
+    x = (_sig(n, np.float64, 11) + 0.002 * t - 3.0).astype(dtype)
+    y = (0.5 * np.roll(x.astype(np.float64), 4) + _sig(n, np.float64, 12)
+         - 0.001 * t).astype(dtype)
+    kw = dict(nperseg=nperseg, nfft=nfft, detrend="linear_lsq")
+    xg, yg = _to_gpu(x, cuda), _to_gpu(y, cuda)
+    if op == "welch":
+        _, got = ib.spectral(ib.OP_WELCH, xg, **kw)
+        _, ref = so.welch(x, **kw)
+    elif op == "csd":
+        _, got = ib.spectral(ib.OP_CSD, xg, yg, complex_output=True, **kw)
+        _, ref = so.csd(x, y, complex_output=True, **kw)
+    elif op == "coherence":
+        _, got = ib.spectral(ib.OP_COHERENCE, xg, yg, **kw)
+        _, ref = so.coherence(x, y, **kw)
+    elif op == "stft":
+        _, _, got = ib.spectral(ib.OP_SPECTROGRAM, xg, mode="complex",
+                                complex_output=True, **kw)
+        _, _, ref = so.spectrogram(x, mode="complex", complex_output=True, **kw)
+    else:
+        _, _, got = ib.spectral(ib.OP_SPECTROGRAM, xg, mode="psd", **kw)
+        _, _, ref = so.spectrogram(x, mode="psd", **kw)
+    assert so.max_rel_err(_np(got), ref) <= TOL[dtype]
+    # and it differs from no detrend (the trend is not negligible)
+    if op == "welch":
+        _, plain = so.welch(x, nperseg=nperseg, nfft=nfft, detrend="none")
+        assert so.max_rel_err(_np(got), plain) > 1e-3
+
+
 # ------------------------------------------------- coherence/periodogram ----
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
 @pytest.mark.parametrize("nperseg,nfft,window,detrend", [

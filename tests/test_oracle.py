@@ -46,6 +46,18 @@ def test_transform_is_the_dft(n):
     assert np.allclose(X, D @ x, atol=1e-8)
 
 
+@pytest.mark.parametrize("M", [2, 7, 256, 1000])
+def test_lsq_detrend_matches_scipy(M):
+    """The native 'linear_lsq' option has no reference counterpart; its
+    restatement is pinned to scipy.signal.detrend(type='linear')."""
+    sig = pytest.importorskip("scipy.signal")
+    rng = np.random.default_rng(M)
+    z = rng.standard_normal((5, M)) + 3.0 + 0.01 * np.arange(M)[None, :]
+    got = z - so.lsq_line(z)
+    ref = sig.detrend(z, axis=1, type="linear")
+    assert np.allclose(got, ref, atol=1e-12, rtol=0)
+
+
 def _cases():
     with open(os.path.join(GOLDEN, "reference_cases.json")) as f:
         return json.load(f)
