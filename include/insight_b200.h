@@ -291,6 +291,13 @@ INSIGHT_B200_API C_Status insight_b200_spectrogram_kernel(void **inputs,
  * [C, n_freq]; onesided must be 1 (the reference's coherence is one-sided). */
 INSIGHT_B200_API C_Status insight_b200_coherence_kernel(void **inputs,
                                                         void **outputs);
+/* "istft" (registered for C32 and C64 Zxx):
+ *   inputs = { out F64 [n_total] or [C, n_total], Zxx, window F64 [nperseg],
+ *              int64_t *nperseg, int64_t *noverlap, int64_t *nfft (each 0 ->
+ *              the reference default), NULL }
+ *   outputs = { out, NULL } */
+INSIGHT_B200_API C_Status insight_b200_istft_kernel(void **inputs,
+                                                    void **outputs);
 
 /* ------------------------------------------------------------------------ */
 /* 3. Host entry points                                                      */
@@ -352,6 +359,25 @@ INSIGHT_B200_API C_Status insight_b200_periodogram(
     const InsightArray *x, double fs, const char *window, int64_t nfft,
     const char *detrend, int return_onesided, const char *scaling,
     InsightArray *f, InsightArray *pxx);
+
+/* Replaces ins::signal::istft (spectral_analysis.h:110-113,
+ * spectral_analysis.cpp:340-457): overlap-add inverse of a one-sided (or
+ * full) complex STFT Zxx (n_freq, n_frames), C32 or C64 (the reference reads
+ * C64), 2-D or a 3-D [C, n_freq, n_frames] batch, any strides; defaults
+ * nfft = 2 (n_freq - 1), nperseg = nfft, noverlap = nperseg / 2; fs is
+ * unused, as in the reference.  out is F64 [n_total] (or [C, n_total]),
+ * n_total = (n_frames - 1) * (nperseg - noverlap) + nperseg; use
+ * insight_b200_istft_shape to size it. */
+INSIGHT_B200_API C_Status insight_b200_istft_shape(const InsightArray *zxx,
+                                                   int64_t nperseg,
+                                                   int64_t noverlap,
+                                                   int64_t nfft,
+                                                   int64_t *n_channels,
+                                                   int64_t *n_total);
+INSIGHT_B200_API C_Status insight_b200_istft(const InsightArray *zxx, double fs,
+                                             const char *window, int64_t nperseg,
+                                             int64_t noverlap, int64_t nfft,
+                                             InsightArray *out);
 
 /* Operation codes of the native entry point. */
 enum {

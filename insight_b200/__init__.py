@@ -2,13 +2,14 @@
 
 Hot path: the reference's ``signal::welch``, ``signal::csd``,
 ``signal::spectrogram`` and ``signal::stft`` (and the compositions
-``coherence`` and ``periodogram``) as one fused sm_100a kernel family behind
+``coherence`` and ``periodogram``, and the inverse ``istft``) as one fused
+sm_100a kernel family behind
 Insight's device-plugin C ABI (include/insight_b200.h).
 """
 from . import _abi  # noqa: F401
 from .signal import (SpectralResult, SpectrogramResult, coherence, csd,  # noqa: F401
-                     finalize_sums, periodogram, spectral, spectral_shape,
-                     spectrogram, stft, welch)
+                     finalize_sums, istft, periodogram, spectral,
+                     spectral_shape, spectrogram, stft, welch)
 
 OP_WELCH = _abi.OP_WELCH
 OP_CSD = _abi.OP_CSD

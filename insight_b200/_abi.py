@@ -109,12 +109,15 @@ EXPORTS = (
     "insight_b200_csd_kernel",
     "insight_b200_spectrogram_kernel",
     "insight_b200_coherence_kernel",
+    "insight_b200_istft_kernel",
     "insight_b200_welch",
     "insight_b200_csd",
     "insight_b200_spectrogram",
     "insight_b200_stft",
     "insight_b200_coherence",
     "insight_b200_periodogram",
+    "insight_b200_istft_shape",
+    "insight_b200_istft",
     "insight_b200_spectral_shape",
     "insight_b200_spectral",
     "insight_b200_finalize_sums",
@@ -139,7 +142,8 @@ def lib() -> ctypes.CDLL:
         L.InitPluginGPU.argtypes = [ctypes.POINTER(CustomRuntimeParams)]
         L.InitPluginGPU.restype = ctypes.c_int
         for n in ("insight_b200_welch_kernel", "insight_b200_csd_kernel",
-                  "insight_b200_spectrogram_kernel", "insight_b200_coherence_kernel"):
+                  "insight_b200_spectrogram_kernel", "insight_b200_coherence_kernel",
+                  "insight_b200_istft_kernel"):
             f = getattr(L, n)
             f.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]
             f.restype = ctypes.c_int
@@ -161,6 +165,12 @@ def lib() -> ctypes.CDLL:
         L.insight_b200_periodogram.argtypes = [
             PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_char_p,
             ctypes.c_int, ctypes.c_char_p, PA, PA]
+        L.insight_b200_istft_shape.argtypes = [
+            PA, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+            ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]
+        L.insight_b200_istft.argtypes = [
+            PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64,
+            ctypes.c_int64, PA]
         PD = ctypes.POINTER(SpectralDesc)
         PI64 = ctypes.POINTER(ctypes.c_int64)
         L.insight_b200_spectral_shape.argtypes = [PD, PA, PI64, PI64, PI64]
@@ -176,7 +186,8 @@ def lib() -> ctypes.CDLL:
         L.insight_b200_welch_noalloc.restype = ctypes.c_int
         for n in ("insight_b200_welch", "insight_b200_csd", "insight_b200_spectrogram",
                   "insight_b200_stft", "insight_b200_coherence",
-                  "insight_b200_periodogram", "insight_b200_spectral_shape",
+                  "insight_b200_periodogram", "insight_b200_istft_shape",
+                  "insight_b200_istft", "insight_b200_spectral_shape",
                   "insight_b200_spectral", "insight_b200_finalize_sums"):
             getattr(L, n).restype = ctypes.c_int
         _lib = L

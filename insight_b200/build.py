@@ -25,10 +25,10 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["spectral_f32.cu", "spectral_f64.cu", "spectral_util.cu",
-              "spectral_noalloc.cu"]
+              "spectral_noalloc.cu", "spectral_istft.cu"]
 CPP_SOURCES = ["launch.cpp", "frontend.cpp", "plugin.cpp", "windows.cpp"]
 HEADERS = ["fft_core.cuh", "spectral_kernels.cuh", "spectral_dispatch.cuh",
-           "spectral_accum_fast.cuh",
+           "spectral_accum_fast.cuh", "spectral_istft.cuh",
            "launch.h", "frontend.h", "windows.h"]
 
 

@@ -75,7 +75,7 @@ struct DeviceState {
   int num_sms = 0;
   cudaStream_t stream = nullptr;
   std::mutex mu;
-  DevBuf scratch, xin, yin, out, win_tmp;
+  DevBuf scratch, xin, yin, out, win_tmp, frames;
   std::map<std::string, DevBuf> tables;
 };
 
@@ -563,6 +563,183 @@ C_Status run(const Call &c) {
 
     put_host_vector(fvec, c.f, "f", stream);
     put_host_vector(tvec, c.t, "t", stream);
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Inverse STFT.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct IstftGeom {
+  int64_t C = 1, F = 0, S = 0, nfft = 0, nperseg = 0, hop = 0, n_total = 0;
+  int64_t cs = 0, fs = 0, ts = 0; // element strides of Zxx
+  bool f64 = false, pack = true;
+};
+
+// Defaults and checks of the reference istft (spectral_analysis.cpp:342-356).
+IstftGeom istft_geom(const IstftCall &c) {
+  IstftGeom g;
+  const InsightArray *z = c.z;
+  check(z != nullptr, "istft: Zxx is undefined");
+  check(z->ndim == 2 || z->ndim == 3,
+        "istft: Zxx must be 2D (or 3D for a batch of channels)");
+  check(z->dtype == INSIGHT_DTYPE_C32 || z->dtype == INSIGHT_DTYPE_C64,
+        "istft: Zxx must be complex (C32 or C64) on the B200 backend");
+  g.f64 = z->dtype == INSIGHT_DTYPE_C64;
+  const int nd = z->ndim;
+  g.F = z->dims[nd - 2];
+  g.S = z->dims[nd - 1];
+  g.fs = z->strides[nd - 2];
+  g.ts = z->strides[nd - 1];
+  if (nd == 3) {
+    g.C = z->dims[0];
+    g.cs = z->strides[0];
+  }
+  check(g.F >= 1 && g.S >= 1, "istft: Zxx is empty");
+  check(g.fs >= 0 && g.ts >= 0 && g.cs >= 0,
+        "istft: negative strides are not supported");
+  g.nfft = c.nfft <= 0 ? 2 * (g.F - 1) : c.nfft;
+  g.nperseg = c.nperseg <= 0 ? g.nfft : c.nperseg;
+  const int64_t noverlap = c.noverlap <= 0 ? g.nperseg / 2 : c.noverlap;
+  g.hop = g.nperseg - noverlap;
+  check(g.hop > 0, "istft: noverlap must be less than nperseg");
+  check(nfft_supported(g.nfft),
+        "istft: nfft must be a power of two in [16, 8192] on the B200 backend "
+        "(got " + std::to_string(g.nfft) + ")");
+  check(g.nperseg <= g.nfft, "istft: nperseg must be <= nfft");
+  g.pack = g.F == g.nfft / 2 + 1 && g.nfft > 2;
+  g.n_total = (g.S - 1) * g.hop + g.nperseg;
+  return g;
+}
+
+} // namespace
+
+C_Status istft_shape(const IstftCall &c, int64_t *n_channels, int64_t *n_total) {
+  try {
+    IstftGeom g = istft_geom(c);
+    if (n_channels)
+      *n_channels = g.C;
+    if (n_total)
+      *n_total = g.n_total;
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+C_Status run_istft(const IstftCall &c) {
+  try {
+    IstftGeom g = istft_geom(c);
+    const InsightArray *z = c.z;
+    InsightArray *out = c.out;
+    check(out != nullptr && out->dtype == INSIGHT_DTYPE_F64,
+          "istft: output must be an F64 array");
+    check(numel(out) == g.C * g.n_total,
+          "istft: output must have " + std::to_string(g.C * g.n_total) +
+              " elements");
+    check(out->ndim == (z->ndim == 3 ? 2 : 1) &&
+              out->dims[out->ndim - 1] == g.n_total,
+          "istft: output must be [n_total] (or [C, n_total] for a batch)");
+    std::vector<double> w;
+    if (c.window_values) {
+      w = *c.window_values;
+      check((int64_t)w.size() == g.nperseg, "istft: window must have nperseg values");
+    } else {
+      try {
+        w = get_window(c.window, g.nperseg, false);
+      } catch (const std::invalid_argument &e) {
+        throw Fail(e.what());
+      }
+    }
+    const bool zgpu = z->device_type == INSIGHT_DEVICE_GPU;
+    const bool ogpu = out->device_type == INSIGHT_DEVICE_GPU;
+    const int dev = zgpu ? z->device_id : (ogpu ? out->device_id : c.default_device);
+    check(!ogpu || out->device_id == dev, "istft: output on a different device");
+    cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    DeviceState &st = device_state(dev);
+    std::lock_guard<std::mutex> lk(st.mu);
+    cudaStream_t stream = c.stream ? c.stream : st.stream;
+
+    IstftDesc d;
+    d.f64 = g.f64;
+    d.C = g.C;
+    d.F = g.F;
+    d.S = g.S;
+    d.nfft = g.nfft;
+    d.nperseg = g.nperseg;
+    d.hop = g.hop;
+    d.n_total = g.n_total;
+    d.pack = g.pack;
+    d.z_cs = g.cs;
+    d.z_fs = g.fs;
+    d.z_ts = g.ts;
+    const size_t zes = dtype_size(z->dtype);
+    if (zgpu) {
+      d.z = base_ptr(z);
+    } else {
+      const int64_t span = (g.C - 1) * g.cs + (g.F - 1) * g.fs + (g.S - 1) * g.ts + 1;
+      ensure(st.xin, span * zes);
+      cuda_check(cudaMemcpyAsync(st.xin.p, base_ptr(z), span * zes,
+                                 cudaMemcpyHostToDevice, stream),
+                 "cudaMemcpyAsync");
+      d.z = st.xin.p;
+    }
+    // tables: window in the compute dtype and in f64, twiddles
+    std::vector<unsigned char> w64(w.size() * 8);
+    std::memcpy(w64.data(), w.data(), w64.size());
+    // the transforms run in f64 for both input precisions
+    if (c.window_values) {
+      auto wb = window_bytes(w, g.nperseg, true);
+      const size_t off = (wb.size() + 15) / 16 * 16; // f64 copy after it
+      ensure(st.win_tmp, off + w64.size());
+      char *p = reinterpret_cast<char *>(st.win_tmp.p);
+      cuda_check(cudaMemcpyAsync(p, wb.data(), wb.size(), cudaMemcpyHostToDevice,
+                                 stream),
+                 "cudaMemcpyAsync");
+      cuda_check(cudaMemcpyAsync(p + off, w64.data(), w64.size(),
+                                 cudaMemcpyHostToDevice, stream),
+                 "cudaMemcpyAsync");
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+      d.win = p;
+      d.win64 = reinterpret_cast<const double *>(p + off);
+    } else {
+      const std::string k = c.window + "|" + std::to_string(g.nperseg);
+      d.win = table(st, std::string("win|d|") + k + "|" + std::to_string(g.nperseg),
+                    window_bytes(w, g.nperseg, true));
+      d.win64 = reinterpret_cast<const double *>(
+          table(st, "win64|" + k, w64));
+    }
+    d.tw = twiddles(st, g.nfft, true);
+    ensure(st.frames, (size_t)g.C * g.S * g.nperseg * 8);
+    d.frames = reinterpret_cast<double *>(st.frames.p);
+    // output: the caller's GPU array, or a device buffer copied back
+    d.o_ss = out->strides[out->ndim - 1];
+    d.o_cs = out->ndim == 2 ? out->strides[0] : 0;
+    int64_t ospan = (g.n_total - 1) * d.o_ss + (g.C - 1) * d.o_cs + 1;
+    if (ogpu) {
+      d.out = reinterpret_cast<double *>(out->data) + out->offset;
+    } else {
+      ensure(st.out, ospan * 8);
+      d.out = reinterpret_cast<double *>(st.out.p);
+    }
+    int64_t nl = 0;
+    cuda_check(launch_istft(d, st.num_sms, stream, &nl), "istft launch");
+    g_launches += nl;
+    if (!ogpu) {
+      cuda_check(cudaMemcpyAsync(reinterpret_cast<double *>(out->data) + out->offset,
+                                 d.out, ospan * 8, cudaMemcpyDeviceToHost, stream),
+                 "cudaMemcpyAsync");
+    }
+    if (c.sync || !zgpu || !ogpu)
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    else
+      cuda_check(cudaGetLastError(), "istft launch");
     return C_SUCCESS;
   } catch (const std::exception &e) {
     set_last_error(e.what());

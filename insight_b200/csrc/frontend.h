@@ -38,7 +38,21 @@ struct Call {
   bool sync = true;
 };
 
+// One inverse STFT (reference ins::signal::istft), see spectral_istft.cuh.
+struct IstftCall {
+  const InsightArray *z = nullptr; // complex [F, S] or [C, F, S]
+  InsightArray *out = nullptr;     // F64 [n_total] or [C, n_total]
+  std::string window = "hann";
+  const std::vector<double> *window_values = nullptr; // registry kernel
+  int64_t nperseg = 0, noverlap = 0, nfft = 0;       // 0 -> reference defaults
+  int default_device = 0;
+  cudaStream_t stream = nullptr;
+  bool sync = true;
+};
+
 C_Status run(const Call &c);
+C_Status run_istft(const IstftCall &c);
+C_Status istft_shape(const IstftCall &c, int64_t *n_channels, int64_t *n_total);
 C_Status shape(const Call &c, int64_t *n_channels, int64_t *n_seg,
                int64_t *n_freq);
 C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums);

@@ -66,6 +66,24 @@ cudaError_t launch(const LaunchDesc &d, void *scratch, int num_sms,
 
 bool nfft_supported(int64_t nfft);
 
+// Inverse STFT (overlap-add) of a complex [C, F, S] array.
+struct IstftDesc {
+  bool f64 = false;         // complex128 input (else complex64)
+  int64_t C = 1, F = 0, S = 0;
+  int64_t nfft = 0, nperseg = 0, hop = 0, n_total = 0;
+  bool pack = true;         // F == nfft/2 + 1: Hermitian frame pairs
+  const void *z = nullptr;  // element (c, k, i) at z[c*z_cs + k*z_fs + i*z_ts]
+  int64_t z_cs = 0, z_fs = 0, z_ts = 0;
+  const void *win = nullptr;    // [nperseg] window (f64: the transform dtype)
+  const double *win64 = nullptr; // [nperseg] window, f64 (normalisation)
+  const void *tw = nullptr;     // [nfft] f64 twiddles
+  double *frames = nullptr;     // scratch [C][S][nperseg]
+  double *out = nullptr;        // element (c, m) at out[c*o_cs + m*o_ss]
+  int64_t o_cs = 0, o_ss = 1;
+};
+cudaError_t launch_istft(const IstftDesc &d, int num_sms, cudaStream_t stream,
+                         int64_t *launches);
+
 // Per-dtype entry points (one translation unit each).
 cudaError_t launch_f32(const LaunchDesc &d, void *scratch, int num_sms,
                        cudaStream_t stream, int64_t *launches);

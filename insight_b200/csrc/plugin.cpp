@@ -526,6 +526,31 @@ C_Status insight_b200_coherence_kernel(void **inputs, void **outputs) {
   return accum_kernel(inputs, outputs, INSIGHT_B200_OP_COHERENCE);
 }
 
+C_Status insight_b200_istft_kernel(void **in, void **out) {
+  if (count_args(in) < 6 || count_args(out) < 1) {
+    set_last_error("istft kernel: expected 6 inputs and 1 output");
+    return C_FAILED;
+  }
+  InsightArray *o = (InsightArray *)out[0];
+  const InsightArray *z = (const InsightArray *)in[1];
+  if (!gpu_array(o) || !gpu_array(z)) {
+    set_last_error("istft kernel: arrays must be GPU arrays");
+    return C_FAILED;
+  }
+  std::vector<double> w;
+  if (!read_window((const InsightArray *)in[2], w))
+    return C_FAILED;
+  ib200::IstftCall c;
+  c.z = z;
+  c.out = o;
+  c.window_values = &w;
+  c.nperseg = *(int64_t *)in[3];
+  c.noverlap = *(int64_t *)in[4];
+  c.nfft = *(int64_t *)in[5];
+  c.sync = true;
+  return ib200::run_istft(c);
+}
+
 C_Status insight_b200_spectrogram_kernel(void **in, void **out) {
   if (count_args(in) < 11 || count_args(out) < 1) {
     set_last_error("spectrogram kernel: expected 11 inputs and 1 output");
@@ -656,6 +681,10 @@ C_Status InitPluginGPU(CustomRuntimeParams *params) {
                               insight_b200_coherence_kernel);
       params->register_kernel("spectrogram", INSIGHT_DEVICE_GPU, dt,
                               insight_b200_spectrogram_kernel);
+      params->register_kernel("istft", INSIGHT_DEVICE_GPU,
+                              dt == INSIGHT_DTYPE_F32 ? INSIGHT_DTYPE_C32
+                                                      : INSIGHT_DTYPE_C64,
+                              insight_b200_istft_kernel);
       params->register_kernel("stft", INSIGHT_DEVICE_GPU, dt,
                               insight_b200_spectrogram_kernel);
     }
@@ -750,6 +779,32 @@ C_Status insight_b200_periodogram(const InsightArray *x, double fs,
   // (spectral_analysis.cpp:189-193)
   return insight_b200_welch(x, fs, window ? window : "boxcar", 256, 0, nfft,
                             detrend, return_onesided, scaling, f, pxx);
+}
+
+C_Status insight_b200_istft_shape(const InsightArray *zxx, int64_t nperseg,
+                                  int64_t noverlap, int64_t nfft,
+                                  int64_t *n_channels, int64_t *n_total) {
+  ib200::IstftCall c;
+  c.z = zxx;
+  c.nperseg = nperseg;
+  c.noverlap = noverlap;
+  c.nfft = nfft;
+  return ib200::istft_shape(c, n_channels, n_total);
+}
+
+C_Status insight_b200_istft(const InsightArray *zxx, double fs,
+                            const char *window, int64_t nperseg,
+                            int64_t noverlap, int64_t nfft, InsightArray *out) {
+  (void)fs; // the reference's istft does not use fs either
+  ib200::IstftCall c;
+  c.z = zxx;
+  c.out = out;
+  c.window = window ? window : "hann";
+  c.nperseg = nperseg;
+  c.noverlap = noverlap;
+  c.nfft = nfft;
+  c.default_device = current_device();
+  return ib200::run_istft(c);
 }
 
 C_Status insight_b200_spectrogram(const InsightArray *x, double fs,

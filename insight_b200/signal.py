@@ -23,8 +23,8 @@ import numpy as np
 from . import _abi
 
 __all__ = ["SpectralResult", "SpectrogramResult", "welch", "csd", "coherence",
-           "periodogram", "spectrogram", "stft", "spectral", "spectral_shape",
-           "finalize_sums"]
+           "periodogram", "spectrogram", "stft", "istft", "spectral",
+           "spectral_shape", "finalize_sums"]
 
 
 @dataclass
@@ -232,6 +232,24 @@ def periodogram(x, fs=1.0, window="boxcar", nfft=None, detrend="constant",
         ctypes.byref(_abi.as_array(f)), ctypes.byref(_abi.as_array(pxx))),
         "periodogram")
     return SpectralResult(f, pxx)
+
+
+def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0):
+    """Inverse STFT (reference istft): F64 signal of length
+    (n_frames - 1) * hop + nperseg.  Zxx is complex (n_freq, n_frames), or a
+    (C, n_freq, n_frames) batch (then the result is (C, n_total))."""
+    za = _abi.as_array(Zxx)
+    c, n = ctypes.c_int64(), ctypes.c_int64()
+    _abi.check(_abi.lib().insight_b200_istft_shape(
+        ctypes.byref(za), int(nperseg or 0), int(noverlap or 0), int(nfft or 0),
+        ctypes.byref(c), ctypes.byref(n)), "istft")
+    shape = (c.value, n.value) if Zxx.ndim == 3 else (n.value,)
+    out = _empty_like_place(Zxx, shape, "float64")
+    _abi.check(_abi.lib().insight_b200_istft(
+        ctypes.byref(za), float(fs), window.encode(), int(nperseg or 0),
+        int(noverlap or 0), int(nfft or 0), ctypes.byref(_abi.as_array(out))),
+        "istft")
+    return out
 
 
 def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,

@@ -201,6 +201,26 @@ int ref_coherence(const void *x, const void *y, int64_t n, int dtype, int mode,
   }
 }
 
+// Reference istft of a C64 (n_freq, n_frames) row-major Zxx given as
+// interleaved (re, im) doubles.
+int ref_istft(const double *z, int64_t n_freq, int64_t n_frames,
+              const char *window, int64_t nperseg, int64_t noverlap,
+              int64_t nfft, double *out, int64_t cap, int64_t *n_out) {
+  try {
+    std::vector<std::complex<double>> zc(n_freq * n_frames);
+    for (size_t i = 0; i < zc.size(); ++i)
+      zc[i] = std::complex<double>(z[2 * i], z[2 * i + 1]);
+    ins::Array za = ins::to_array(zc, ins::Shape({n_freq, n_frames}),
+                                  ins::CPUPlace());
+    ins::Array r = ins::signal::istft(za, 1.0, window, nperseg, noverlap, nfft);
+    *n_out = copy_out(r, out, cap);
+    return 0;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
 // Reference spectrogram; S is returned (n_seg, n_freq) row-major (the
 // reference returns a transposed view of an (n_freq, n_seg) buffer).
 int ref_spectrogram(const void *x, int64_t n, int dtype, double fs,

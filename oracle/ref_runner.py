@@ -45,6 +45,8 @@ def lib():
                                     ctypes.c_int, ctypes.c_double, ctypes.c_char_p, I,
                                     I, I, ctypes.c_char_p, ctypes.c_int,
                                     ctypes.c_char_p, P, P, I, ctypes.POINTER(I)]
+        L.ref_istft.argtypes = [P, I, I, ctypes.c_char_p, I, I, I, P, I,
+                                ctypes.POINTER(I)]
         L.ref_spectrogram.argtypes = [ctypes.c_void_p, I, ctypes.c_int, ctypes.c_double,
                                       ctypes.c_char_p, I, I, I, ctypes.c_char_p,
                                       ctypes.c_int, ctypes.c_char_p, ctypes.c_int, P, P,
@@ -125,6 +127,25 @@ def periodogram(x, fs=1.0, window="boxcar", nfft=0, detrend="constant",
     """Reference periodogram (welch with nperseg 256): returns (f, Pxx) F64."""
     return _coh(2, x, None, fs, window, 256, 0, nfft, detrend, return_onesided,
                 scaling)
+
+
+def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0):
+    """Reference istft of a complex (n_freq, n_frames) array: F64 signal."""
+    L = lib()
+    z = np.ascontiguousarray(Zxx, dtype=np.complex128)
+    F, S = z.shape
+    nf_ = nfft if nfft > 0 else 2 * (F - 1)
+    nps = nperseg if nperseg > 0 else nf_
+    cap = (S + 1) * nps + nf_ + 16
+    out = np.zeros(cap)
+    n = ctypes.c_int64()
+    P = ctypes.POINTER(ctypes.c_double)
+    rc = L.ref_istft(z.view(np.float64).ctypes.data_as(P), F, S, window.encode(),
+                     nperseg, noverlap, nfft, out.ctypes.data_as(P), cap,
+                     ctypes.byref(n))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    return out[:n.value].copy()
 
 
 def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,

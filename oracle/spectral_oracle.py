@@ -257,6 +257,45 @@ def stft(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
                        "complex", complex_output=complex_output, win=win)
 
 
+def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0,
+          reference_mirror=False):
+    """Reference istft (:340-457): per frame Re(ifft(full, nfft))[:nperseg]
+    * w, where full mirrors bins 1..F-2 as conjugates when F == nfft/2 + 1
+    and nfft > 2; overlap-add with hop = nperseg - noverlap; division by the
+    overlap-added w^2 where it exceeds 1e-10.  fs is unused (as there).
+
+    reference_mirror=True reproduces what the reference computes instead of
+    the mirror it intends: it conjugates the view col[1:F-1] with an
+    elementwise op that reads from the storage base and ignores the view's
+    offset (:384-389), so full[nfft-m] = conj(Z[m-1]) rather than
+    conj(Z[m]).  The backend computes the intended inverse."""
+    Z = np.asarray(Zxx, dtype=np.complex128)
+    F, S = Z.shape
+    if nfft <= 0:
+        nfft = 2 * (F - 1)
+    if nperseg <= 0:
+        nperseg = nfft
+    if noverlap <= 0:
+        noverlap = nperseg // 2
+    win = get_window(window, nperseg, False)
+    hop = nperseg - noverlap
+    if F == nfft // 2 + 1 and nfft > 2:
+        lo = 0 if reference_mirror else 1
+        full = np.concatenate([Z, np.conj(Z[lo:lo + F - 2][::-1])], axis=0)
+    else:
+        full = Z
+    seg = np.fft.ifft(full, n=nfft, axis=0).real[:nperseg] * win[:, None]
+    n_total = (S - 1) * hop + nperseg
+    out = np.zeros(n_total)
+    norm = np.zeros(n_total)
+    for i in range(S):
+        out[i * hop:i * hop + nperseg] += seg[:, i]
+        norm[i * hop:i * hop + nperseg] += win * win
+    m = np.abs(norm) > 1e-10
+    out[m] /= norm[m]
+    return out
+
+
 def max_rel_err(got, ref):
     """max_k |got - ref| / max_k |ref| (the parity metric)."""
     got = np.asarray(got)

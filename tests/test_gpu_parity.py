@@ -251,6 +251,90 @@ def test_periodogram(cuda, dtype, window, nfft, scaling, onesided):
     assert so.max_rel_err(_np(r.Pxx), p) <= TOL[dtype]
 
 
+# ------------------------------------------------------------------ istft ----
+def _ola_norm(n_total, S, nperseg, hop, window):
+    w2 = so.get_window(window, nperseg) ** 2
+    nrm = np.zeros(n_total)
+    for i in range(S):
+        nrm[i * hop:i * hop + nperseg] += w2
+    return nrm
+
+
+def _istft_err(got, ref, S, nperseg, hop, window):
+    """max_rel_err of the overlap-added frames before the division by the
+    summed squared window: where that sum is tiny (the window's ends) the
+    division amplifies any transform's rounding, in the reference as well."""
+    nrm = _ola_norm(len(ref), S, nperseg, hop, window)
+    return so.max_rel_err(np.asarray(got) * nrm, np.asarray(ref) * nrm)
+
+
+@pytest.mark.parametrize("cdtype", [np.complex64, np.complex128])
+@pytest.mark.parametrize("L,stft_ov,nperseg,noverlap,nfft,window", [
+    (128, 64, 0, 0, 0, "hann"),            # reference defaults
+    (2048, 1536, 2048, 1536, 0, "hann"),
+    (256, 192, 256, 192, 0, "hamming"),
+    (100, 50, 100, 50, 128, "hann"),       # nperseg < nfft (truncation)
+    (16, 8, 16, 8, 0, "blackman"),
+    (8192, 4096, 8192, 4096, 0, "hann")])
+def test_istft(cuda, cdtype, L, stft_ov, nperseg, noverlap, nfft, window):
+    import torch
+    x = _sig(6 * max(L, 128) + 77, np.float64, 13)
+    _, _, z = so.stft(x, window=window, nperseg=L, noverlap=stft_ov,
+                      nfft=nfft or L, complex_output=True)
+    z = z.astype(cdtype)
+    kw = dict(window=window, nperseg=nperseg, noverlap=noverlap, nfft=nfft)
+    got = _np(ib.istft(torch.from_numpy(np.ascontiguousarray(z)).to(cuda), **kw))
+    ref = so.istft(z, **kw)
+    assert got.shape == ref.shape
+    nps = nperseg or 2 * (z.shape[0] - 1)
+    hop = nps - (noverlap or nps // 2)
+    err = _istft_err(got, ref, z.shape[1], nps, hop, window)
+    assert err <= (1e-5 if cdtype == np.complex64 else 1e-12), err
+
+
+@pytest.mark.parametrize("layout", ["batch", "strided_view", "host", "two_sided"])
+def test_istft_layouts(cuda, layout):
+    import torch
+    C, L, ov = 3, 512, 384
+    X = np.stack([_sig(9000, np.float64, 20 + c) for c in range(C)])
+    zs = [so.stft(X[c], nperseg=L, noverlap=ov, complex_output=True)[2]
+          for c in range(C)]
+    Z = np.stack(zs)                                  # (C, F, S) complex128
+    kw = dict(nperseg=L, noverlap=ov)
+    if layout == "two_sided":
+        step, S = so.framing(9000, L, ov, True)
+        segs = so._segments(X[0], L, step, S) * so.get_window("hann", L)[None, :]
+        zf = np.fft.fft(segs, axis=1).T               # (L, S): no mirroring
+        got = _np(ib.istft(torch.from_numpy(np.ascontiguousarray(zf)).to(cuda),
+                           nfft=L, **kw))
+        ref = so.istft(zf, nfft=L, **kw)
+        assert _istft_err(got, ref, zf.shape[1], L, L - ov, "hann") <= 1e-12
+        return
+    if layout == "batch":
+        zin = torch.from_numpy(Z).to(cuda)
+    elif layout == "strided_view":                    # (C, F, S) view of (C, S, F)
+        zin = torch.from_numpy(np.ascontiguousarray(Z.transpose(0, 2, 1))).to(
+            cuda).transpose(1, 2)
+    else:
+        zin = Z
+    got = _np(ib.istft(zin, **kw))
+    assert got.shape[0] == C
+    for c in range(C):
+        ref = so.istft(Z[c], **kw)
+        assert _istft_err(got[c], ref, Z.shape[2], L, L - ov, "hann") <= 1e-12
+
+
+def test_istft_errors(cuda):
+    import torch
+    z = torch.zeros((65, 10), dtype=torch.complex128, device=cuda)
+    with pytest.raises(RuntimeError, match="noverlap must be less than nperseg"):
+        ib.istft(z, nperseg=64, noverlap=64)
+    with pytest.raises(RuntimeError, match="nperseg must be <= nfft"):
+        ib.istft(z, nperseg=256)
+    with pytest.raises(RuntimeError, match="must be complex"):
+        ib.istft(torch.zeros((65, 10), dtype=torch.float64, device=cuda))
+
+
 # ------------------------------------------------------ spectrogram/stft ----
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
 @pytest.mark.parametrize("mode", ["psd", "complex", "magnitude"])
@@ -393,6 +477,8 @@ def test_plugin_registry_kernels(cuda):
     for name in ("welch", "csd", "coherence", "spectrogram", "stft"):
         for dt in (_abi.DT_F32, _abi.DT_F64):
             assert (name, _abi.DEV_GPU, dt) in reg
+    for dt in (_abi.DT_C32, _abi.DT_C64):
+        assert ("istft", _abi.DEV_GPU, dt) in reg
     assert iface.device_memory_allocate and iface.get_last_error
 
     x = _sig(40000, np.float32, 8)
