@@ -15,6 +15,8 @@ Other workloads (--workload):
   csd         512 f32 channel pairs x 2^21 given as transposed (N, C) views,
               nperseg 2048, 50%, hann, complex64 cross spectra
   coherence   the csd workload through signal::coherence (F64 Cxy)
+  istft       the stft workload's complex64 output back to F64 signals
+              (GSamples/s of reconstructed samples)
   welch_long  one f32 signal of 2^30 samples, nperseg 8192, 50%, blackman,
               sharded by segment range over the ranks with one NCCL
               all-reduce of the F64 partial sums (strong scaling)
@@ -70,6 +72,11 @@ WORKLOADS = {
                       desc=("signal::coherence {C} f32 pairs x 2^21 per GPU as "
                             "transposed (samples, channels) views, nperseg "
                             "2048, 50%, hann (one pass over x and y)")),
+    "istft": dict(op="istft", C=64, N=1 << 22, L=2048, H=512, window="hann",
+                  dtype="f32", fs=1.0e4, desc=(
+                      "signal::istft of the stft workload's complex64 "
+                      "({C}, 1025, 8189) back to {C} ch x 4194304 F64 samples "
+                      "per GPU, nperseg 2048, hop 512, hann")),
     "welch_long": dict(op="welch", C=1, N=1 << 30, L=8192, H=4096,
                        window="blackman", dtype="f32", fs=1.0, detrend="constant",
                        desc=("signal::welch one f32 signal of 2^30 samples, "
@@ -149,7 +156,7 @@ def make_inputs(torch, dev, w, rank, C):
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     N, fs = w["N"], w["fs"]
-    if w["op"] == "stft":
+    if w["op"] in ("stft", "istft"):
         x = torch.randn((C, N), generator=g, device=dev, dtype=torch.float32)
         t = torch.arange(N, device=dev, dtype=torch.float64) / fs
         T = N / fs
@@ -385,7 +392,23 @@ def run_ours(args, w):
         two = op in ("csd", "coherence")
         samples = C * N * (2 if two else 1) * world
         in_bytes = C * N * x.element_size() * (2 if two else 1)
-        if op == "stft":
+        if op == "istft":
+            # input: the stft of the seeded signal (outside the timed region)
+            z = torch.empty((C, F, S), dtype=torch.complex64, device=dev)
+            ib.spectral(ib.OP_STFT, x, out=z, complex_output=True,
+                        **{k: v for k, v in kw.items() if k not in ("stream",)})
+            torch.cuda.synchronize()
+            x = z
+            n_total = (S - 1) * H + L
+            out = torch.empty((C, n_total), dtype=torch.float64, device=dev)
+            samples = C * n_total * world
+            in_bytes = C * F * S * 8
+            out_bytes = C * n_total * 8
+            nfft_work = C * S
+            def call(xin, yin, o):
+                ib.istft(xin, window=w["window"], nperseg=L, noverlap=L - H,
+                         out=o, stream=stream, sync=False)
+        elif op == "stft":
             out = torch.empty((C, F, S), dtype=torch.complex64, device=dev)
             out_bytes = C * F * S * 8
             nfft_work = C * S

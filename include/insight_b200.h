@@ -378,6 +378,12 @@ INSIGHT_B200_API C_Status insight_b200_istft(const InsightArray *zxx, double fs,
                                              const char *window, int64_t nperseg,
                                              int64_t noverlap, int64_t nfft,
                                              InsightArray *out);
+/* insight_b200_istft on a caller stream (cudaStream_t of Zxx's device, NULL
+ * -> the backend's own); returns after enqueueing when sync == 0 and Zxx and
+ * out are GPU arrays. */
+INSIGHT_B200_API C_Status insight_b200_istft_async(
+    const InsightArray *zxx, const char *window, int64_t nperseg,
+    int64_t noverlap, int64_t nfft, InsightArray *out, void *stream, int sync);
 
 /* Operation codes of the native entry point. */
 enum {

@@ -118,6 +118,7 @@ EXPORTS = (
     "insight_b200_periodogram",
     "insight_b200_istft_shape",
     "insight_b200_istft",
+    "insight_b200_istft_async",
     "insight_b200_spectral_shape",
     "insight_b200_spectral",
     "insight_b200_finalize_sums",
@@ -171,6 +172,10 @@ def lib() -> ctypes.CDLL:
         L.insight_b200_istft.argtypes = [
             PA, ctypes.c_double, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64,
             ctypes.c_int64, PA]
+        L.insight_b200_istft_async.argtypes = [
+            PA, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, PA,
+            ctypes.c_void_p, ctypes.c_int]
+        L.insight_b200_istft_async.restype = ctypes.c_int
         PD = ctypes.POINTER(SpectralDesc)
         PI64 = ctypes.POINTER(ctypes.c_int64)
         L.insight_b200_spectral_shape.argtypes = [PD, PA, PI64, PI64, PI64]

@@ -807,6 +807,23 @@ C_Status insight_b200_istft(const InsightArray *zxx, double fs,
   return ib200::run_istft(c);
 }
 
+C_Status insight_b200_istft_async(const InsightArray *zxx, const char *window,
+                                  int64_t nperseg, int64_t noverlap,
+                                  int64_t nfft, InsightArray *out, void *stream,
+                                  int sync) {
+  ib200::IstftCall c;
+  c.z = zxx;
+  c.out = out;
+  c.window = window ? window : "hann";
+  c.nperseg = nperseg;
+  c.noverlap = noverlap;
+  c.nfft = nfft;
+  c.default_device = current_device();
+  c.stream = (cudaStream_t)stream;
+  c.sync = sync != 0;
+  return ib200::run_istft(c);
+}
+
 C_Status insight_b200_spectrogram(const InsightArray *x, double fs,
                                   const char *window, int64_t nperseg,
                                   int64_t noverlap, int64_t nfft,

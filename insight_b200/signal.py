@@ -234,20 +234,26 @@ def periodogram(x, fs=1.0, window="boxcar", nfft=None, detrend="constant",
     return SpectralResult(f, pxx)
 
 
-def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0):
+def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0, *,
+          out=None, stream=None, sync=True):
     """Inverse STFT (reference istft): F64 signal of length
     (n_frames - 1) * hop + nperseg.  Zxx is complex (n_freq, n_frames), or a
-    (C, n_freq, n_frames) batch (then the result is (C, n_total))."""
+    (C, n_freq, n_frames) batch (then the result is (C, n_total)).  fs is
+    unused, as in the reference."""
     za = _abi.as_array(Zxx)
-    c, n = ctypes.c_int64(), ctypes.c_int64()
-    _abi.check(_abi.lib().insight_b200_istft_shape(
-        ctypes.byref(za), int(nperseg or 0), int(noverlap or 0), int(nfft or 0),
-        ctypes.byref(c), ctypes.byref(n)), "istft")
-    shape = (c.value, n.value) if Zxx.ndim == 3 else (n.value,)
-    out = _empty_like_place(Zxx, shape, "float64")
-    _abi.check(_abi.lib().insight_b200_istft(
-        ctypes.byref(za), float(fs), window.encode(), int(nperseg or 0),
-        int(noverlap or 0), int(nfft or 0), ctypes.byref(_abi.as_array(out))),
+    if out is None:
+        c, n = ctypes.c_int64(), ctypes.c_int64()
+        _abi.check(_abi.lib().insight_b200_istft_shape(
+            ctypes.byref(za), int(nperseg or 0), int(noverlap or 0),
+            int(nfft or 0), ctypes.byref(c), ctypes.byref(n)), "istft")
+        shape = (c.value, n.value) if Zxx.ndim == 3 else (n.value,)
+        out = _empty_like_place(Zxx, shape, "float64")
+    st = None
+    if stream is not None:
+        st = ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    _abi.check(_abi.lib().insight_b200_istft_async(
+        ctypes.byref(za), window.encode(), int(nperseg or 0), int(noverlap or 0),
+        int(nfft or 0), ctypes.byref(_abi.as_array(out)), st, 1 if sync else 0),
         "istft")
     return out
 

@@ -324,6 +324,25 @@ def test_istft_layouts(cuda, layout):
         assert _istft_err(got[c], ref, Z.shape[2], L, L - ov, "hann") <= 1e-12
 
 
+def test_istft_reference_signature_entry(cuda):
+    """insight_b200_istft (the reference's argument list) by window name."""
+    import ctypes
+    import torch
+    from insight_b200 import _abi
+    x = _sig(5000, np.float64, 30)
+    _, _, z = so.stft(x, window="hamming", nperseg=256, noverlap=128,
+                      complex_output=True)
+    zt = torch.from_numpy(np.ascontiguousarray(z)).to(cuda)
+    n_total = (z.shape[1] - 1) * 128 + 256
+    out = torch.empty(n_total, dtype=torch.float64, device=cuda)
+    rc = _abi.lib().insight_b200_istft(
+        ctypes.byref(_abi.as_array(zt)), 1.0, b"hamming", 256, 128, 0,
+        ctypes.byref(_abi.as_array(out)))
+    assert rc == 0, _abi.last_error()
+    ref = so.istft(z, window="hamming", nperseg=256, noverlap=128)
+    assert _istft_err(_np(out), ref, z.shape[1], 256, 128, "hamming") <= 1e-12
+
+
 def test_istft_errors(cuda):
     import torch
     z = torch.zeros((65, 10), dtype=torch.complex128, device=cuda)
