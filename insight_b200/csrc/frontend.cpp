@@ -74,6 +74,12 @@ struct DeviceState {
   int dev = 0;
   int num_sms = 0;
   cudaStream_t stream = nullptr;
+  // host-I/O pipeline: channel chunks alternate over these streams so the
+  // host->device copy of one chunk, the kernel of another and the
+  // device->host copy of a third overlap (PCIe is full duplex)
+  static constexpr int kPipe = 3;
+  cudaStream_t pipe[kPipe] = {};
+  cudaEvent_t pipe_start = nullptr;
   std::mutex mu;
   DevBuf scratch, xin, yin, out, win_tmp, frames;
   std::map<std::string, DevBuf> tables;
@@ -412,7 +418,18 @@ C_Status run(const Call &c) {
                  "cudaMemcpyAsync");
       return buf.p;
     };
-    d.x = stage(xv, st.xin);
+    // Host input and host output of a channel batch of spectrogram / stft:
+    // copies and launches are pipelined per channel chunk (below), so the
+    // input is only reserved here.
+    const bool host_pipe = !acc && !xv.gpu && c.out &&
+                           c.out->device_type != INSIGHT_DEVICE_GPU &&
+                           xv.C >= 2 && xv.cs >= (xv.N - 1) * xv.ss + 1;
+    if (host_pipe) {
+      ensure(st.xin, xv.span * dtype_size(xv.dtype));
+      d.x = st.xin.p;
+    } else {
+      d.x = stage(xv, st.xin);
+    }
     d.y = two ? stage(yv, st.yin) : nullptr;
 
     // Tables.
@@ -540,6 +557,59 @@ C_Status run(const Call &c) {
     d.o_cs = o_cs;
     d.o_rs = o_rs;
     d.o_ts = o_ts;
+
+    // Pipelined host I/O (see host_pipe): chunk j of channels [c0, c1) is
+    // copied in, transformed and copied out on stream j % kPipe.
+    const int64_t span_c = span - (xv.C - 1) * o_cs; // one channel's output
+    if (host_pipe && o_cs >= span_c) {
+      const size_t xes = dtype_size(xv.dtype);
+      const int64_t xspan_c = (xv.N - 1) * xv.ss + 1;
+      const int64_t K = std::min<int64_t>(xv.C, 8);
+      for (int i = 0; i < DeviceState::kPipe; ++i)
+        if (!st.pipe[i])
+          cuda_check(cudaStreamCreateWithFlags(&st.pipe[i], cudaStreamNonBlocking),
+                     "cudaStreamCreate");
+      if (!st.pipe_start)
+        cuda_check(cudaEventCreateWithFlags(&st.pipe_start, cudaEventDisableTiming),
+                   "cudaEventCreate");
+      // table uploads above were issued on `stream`
+      cuda_check(cudaEventRecord(st.pipe_start, stream), "cudaEventRecord");
+      const char *xh = base_ptr(xv.a);
+      char *oh = reinterpret_cast<char *>(out->data) + out->offset * (int64_t)oes;
+      int64_t nl = 0;
+      for (int64_t j = 0; j < K; ++j) {
+        const int64_t c0 = xv.C * j / K, c1 = xv.C * (j + 1) / K;
+        cudaStream_t ps = st.pipe[j % DeviceState::kPipe];
+        if (j < DeviceState::kPipe)
+          cuda_check(cudaStreamWaitEvent(ps, st.pipe_start, 0), "cudaStreamWaitEvent");
+        const size_t xoff = (size_t)(c0 * xv.cs) * xes;
+        const size_t xlen = (size_t)((c1 - c0 - 1) * xv.cs + xspan_c) * xes;
+        cuda_check(cudaMemcpyAsync(static_cast<char *>(st.xin.p) + xoff, xh + xoff,
+                                   xlen, cudaMemcpyHostToDevice, ps),
+                   "cudaMemcpyAsync");
+        LaunchDesc dj = d;
+        dj.C = c1 - c0;
+        dj.x = static_cast<const char *>(st.xin.p) + xoff;
+        dj.out = static_cast<char *>(obase) + (size_t)(c0 * o_cs) * oes;
+        cuda_check(launch(dj, nullptr, st.num_sms, ps, &nl), "kernel launch");
+        const size_t ooff = (size_t)(c0 * o_cs) * oes;
+        const size_t olen = (size_t)((c1 - c0 - 1) * o_cs + span_c) * oes;
+        cuda_check(cudaMemcpyAsync(oh + ooff, static_cast<char *>(obase) + ooff, olen,
+                                   cudaMemcpyDeviceToHost, ps),
+                   "cudaMemcpyAsync");
+      }
+      g_launches += nl;
+      for (int i = 0; i < DeviceState::kPipe; ++i)
+        cuda_check(cudaStreamSynchronize(st.pipe[i]), "cudaStreamSynchronize");
+      put_host_vector(fvec, c.f, "f", stream);
+      put_host_vector(tvec, c.t, "t", stream);
+      return C_SUCCESS;
+    }
+    if (host_pipe) // output channels interleave: one copy of the whole input
+      cuda_check(cudaMemcpyAsync(st.xin.p, base_ptr(xv.a),
+                                 xv.span * dtype_size(xv.dtype),
+                                 cudaMemcpyHostToDevice, stream),
+                 "cudaMemcpyAsync");
 
     // Scratch and launch.
     const size_t sb = scratch_bytes(d, st.num_sms);

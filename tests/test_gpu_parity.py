@@ -431,6 +431,22 @@ def test_batched_layouts(cuda, layout):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("complex_output", [True, False])
+def test_stft_host_batch_pipelined(cuda, complex_output):
+    """Host input and host output of a channel batch: the copies and kernels
+    run per channel chunk on several streams."""
+    C, N, L = 11, 40000, 1024
+    rng = np.random.default_rng(17)
+    X = rng.standard_normal((C, N)).astype(np.float32)
+    f, t, z = ib.spectral(ib.OP_STFT, X, nperseg=L, noverlap=768,
+                          complex_output=complex_output)
+    assert isinstance(z, np.ndarray)
+    for c in range(C):
+        _, _, zr = so.stft(X[c], nperseg=L, noverlap=768,
+                           complex_output=complex_output)
+        assert so.max_rel_err(z[c], zr) <= 1e-5
+
+
 def test_storage_offset_view(cuda):
     import torch
     base = _to_gpu(_sig(50000, np.float64, 4), cuda)
