@@ -65,8 +65,10 @@ __device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
 // the samples are loaded straight into registers.
 // TWM: Stockham twiddles from the global table (0), from per-thread rows of
 // the first twiddle of each butterfly (1), or from full per-thread rows (2).
+// Coherence CTAs (256 threads) are register-capped at 128 so that two fit
+// on an SM next to each other.
 template <typename T, int L, int E, int G, int SH, int TWM, int MODE, bool STG>
-__global__ void __launch_bounds__(G *(L / E))
+__global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
     accum_fast_kernel(const SpecArgs<T> p) {
   using V = typename V2T<T>::type;
   using PL = Plan<L, E>;

@@ -343,6 +343,29 @@ constexpr AccShape acc_fast_shape() {
   return {0, 0};
 }
 
+// Resident CTAs per SM of one fast accumulate instantiation (sets its
+// dynamic shared-memory limit on first use; 0 on error).
+template <typename T, int L, int MODE, int SH, bool STG>
+int acc_fast_blocks_per_sm() {
+  constexpr int E = values_per_thread<T>(L);
+  constexpr int P = L / E;
+  constexpr AccShape AS = acc_fast_shape<T, L, STG, MODE>();
+  auto kern = accum_fast_kernel<T, L, E, AS.G, SH, AS.twm, MODE, STG>;
+  const size_t smem = acc_fast_smem<T, L>(AS.G, AS.twm, STG, MODE);
+  static int blocks_per_sm = -1;
+  if (blocks_per_sm < 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return 0;
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, AS.G * P,
+                                                      smem) != cudaSuccess)
+      return 0;
+    blocks_per_sm = std::max(nb, 1);
+  }
+  return blocks_per_sm;
+}
+
 template <typename T, int L, int MODE, int SH, bool STG>
 cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
                               cudaStream_t stream, int64_t *launches) {
@@ -352,18 +375,10 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
   constexpr int G = AS.G;
   auto kern = accum_fast_kernel<T, L, E, G, SH, AS.twm, MODE, STG>;
   const size_t smem = acc_fast_smem<T, L>(G, AS.twm, STG, MODE);
-  static int blocks_per_sm = -1;
-  if (blocks_per_sm < 0) {
-    cudaError_t e = cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess)
-      return e;
-    int nb = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G * P, smem);
-    if (e != cudaSuccess)
-      return e;
-    blocks_per_sm = std::max(nb, 1);
-  }
+  const int blocks_per_sm = acc_fast_blocks_per_sm<T, L, MODE, SH, STG>();
+  if (blocks_per_sm == 0)
+    return cudaGetLastError() != cudaSuccess ? cudaErrorInvalidValue
+                                             : cudaErrorInvalidConfiguration;
   SpecArgs<T> a = make_args<T>(d, scratch);
   // Flat split: one CTA per resident slot, each with the same number of
   // transforms (to within one); CTA b's partial of channel c is slot b + c.
@@ -405,48 +420,52 @@ bool segments_aligned16(const LaunchDesc &d, int L) {
   return ok;
 }
 
+// cp.async staging where the segments are 16-byte aligned and it keeps as
+// many resident threads per SM as the unstaged kernel (its buffers can cost
+// a CTA per SM, e.g. coherence at 256 threads).
+template <typename T, int L, int MODE, int SH>
+cudaError_t run_accum_fast_pick(const LaunchDesc &d, void *scratch, int num_sms,
+                                cudaStream_t stream, int64_t *launches) {
+  constexpr AccShape S0 = acc_fast_shape<T, L, false, MODE>();
+  constexpr AccShape S1 = acc_fast_shape<T, L, true, MODE>();
+  if constexpr (S1.G > 0 && S1.G >= S0.G) {
+    if (segments_aligned16<T, MODE>(d, L)) {
+      const int b1 = acc_fast_blocks_per_sm<T, L, MODE, SH, true>();
+      const int b0 = acc_fast_blocks_per_sm<T, L, MODE, SH, false>();
+      if (b1 > 0 && b1 * S1.G >= b0 * S0.G)
+        return run_accum_fast_sh<T, L, MODE, SH, true>(d, scratch, num_sms,
+                                                       stream, launches);
+    }
+  }
+  return run_accum_fast_sh<T, L, MODE, SH, false>(d, scratch, num_sms, stream,
+                                                  launches);
+}
+
 template <typename T, int L, int MODE>
 cudaError_t run_accum_any(const LaunchDesc &d, void *scratch, int num_sms,
                           cudaStream_t stream, int64_t *launches) {
   constexpr int E = values_per_thread<T>(L);
   constexpr int R0 = Plan<L, E>::radix(0);
   constexpr AccShape S0 = acc_fast_shape<T, L, false, MODE>();
-  constexpr AccShape S1 = acc_fast_shape<T, L, true, MODE>();
-  // staging only where it costs no transform groups
-  constexpr bool STG_OK = S1.G > 0 && S1.G >= S0.G;
   if constexpr (S0.G > 0 && !(MODE != ACC_PSD && packs_xy<T, L>())) {
     const bool ok = d.x_ss == 1 && (MODE == ACC_PSD || d.y_ss == 1) &&
                     d.nperseg == d.nfft && d.dc_mode <= 1;
     if (ok) {
-      int sh = 0;
+      // overlap reuse: hop = SH * L/R0 lets segment b take samples from a
       constexpr int Q = L / R0;
-      if (d.step % Q == 0) {
-        const int64_t v = d.step / Q;
-        if (R0 >= 4 && v == R0 / 4)
-          sh = R0 / 4;
-        else if (R0 >= 2 && v == R0 / 2)
-          sh = R0 / 2;
-      }
-      const bool stg = STG_OK && segments_aligned16<T, MODE>(d, L);
-      auto go = [&](auto shIC, auto stgIC) {
-        return run_accum_fast_sh<T, L, MODE, decltype(shIC)::value,
-                                 decltype(stgIC)::value>(d, scratch, num_sms,
-                                                         stream, launches);
-      };
-      using F = std::integral_constant<bool, false>;
-      using Tr = std::integral_constant<bool, STG_OK>;
+      const int64_t v = d.step % Q == 0 ? d.step / Q : -1;
       if constexpr (R0 >= 4) {
-        if (sh == R0 / 4)
-          return stg ? go(std::integral_constant<int, R0 / 4>{}, Tr{})
-                     : go(std::integral_constant<int, R0 / 4>{}, F{});
+        if (v == R0 / 4)
+          return run_accum_fast_pick<T, L, MODE, R0 / 4>(d, scratch, num_sms,
+                                                         stream, launches);
       }
       if constexpr (R0 >= 2) {
-        if (sh == R0 / 2)
-          return stg ? go(std::integral_constant<int, R0 / 2>{}, Tr{})
-                     : go(std::integral_constant<int, R0 / 2>{}, F{});
+        if (v == R0 / 2)
+          return run_accum_fast_pick<T, L, MODE, R0 / 2>(d, scratch, num_sms,
+                                                         stream, launches);
       }
-      return stg ? go(std::integral_constant<int, 0>{}, Tr{})
-                 : go(std::integral_constant<int, 0>{}, F{});
+      return run_accum_fast_pick<T, L, MODE, 0>(d, scratch, num_sms, stream,
+                                                launches);
     }
   }
   return run_accum<T, L, MODE>(d, scratch, num_sms, stream, launches);
