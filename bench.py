@@ -527,10 +527,11 @@ def run_ours(args, w):
 
 
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the
-# ncu capture summarised in profiles/ (measured on 8 channels, scaled by the
-# channel count: the traffic is per channel).
+# ncu capture summarised in profiles/ (measured on 8 channels and scaled by
+# the channel count: the traffic is per channel; output bytes still in L2 at
+# the end of the small capture are missing, so this is a lower bound).
 TRAFFIC = {
-    "stft": lambda C: (149_994_496 + 504_300_544) / 8 * C,
+    "stft": lambda C: (152_996_096 + 497_428_480) / 8 * C,
 }
 
 

@@ -28,7 +28,7 @@ CU_SOURCES = ["spectral_f32.cu", "spectral_f64.cu", "spectral_util.cu",
               "spectral_noalloc.cu", "spectral_istft.cu"]
 CPP_SOURCES = ["launch.cpp", "frontend.cpp", "plugin.cpp", "windows.cpp"]
 HEADERS = ["fft_core.cuh", "spectral_kernels.cuh", "spectral_dispatch.cuh",
-           "spectral_accum_fast.cuh", "spectral_istft.cuh",
+           "spectral_accum_fast.cuh", "spectral_istft.cuh", "spectral_stft_ws.cuh",
            "launch.h", "frontend.h", "windows.h"]
 
 

@@ -4,24 +4,13 @@
 #include "launch.h"
 #include "spectral_kernels.cuh"
 #include "spectral_accum_fast.cuh"
+#include "spectral_stft_ws.cuh"
 
 #include <algorithm>
 #include <type_traits>
 
 namespace ib200 {
 
-// Values per thread: 16 (f32) / 8 (f64) for long transforms; short
-// transforms keep at least 32 threads per group where possible.
-template <typename T> __host__ __device__ constexpr int values_per_thread(int L) {
-  const int big = std::is_same<T, float>::value ? 16 : 8;
-  const int minE = 2;
-  int e = L / 32;
-  if (e > big)
-    e = big;
-  if (e < minE)
-    e = minE;
-  return e;
-}
 
 // Transform groups per CTA of the store kernel: about 16K (f32) / 8K (f64)
 // staged values, at most 8 groups, 1024 threads, and one group when a group
@@ -239,9 +228,70 @@ cudaError_t run_stft_fast_sh(const LaunchDesc &d, int num_sms,
   return cudaGetLastError();
 }
 
+// Warp-specialised variant (spectral_stft_ws.cuh) where its shape fits.
+#ifndef IB200_STFT_WS
+#define IB200_STFT_WS 1
+#endif
+template <typename T, int L> constexpr int stft_ws_mode() {
+  using SS = StftWsShape<T, L>;
+  if constexpr (!IB200_STFT_WS || !SS::ok) {
+    return 0;
+  } else {
+    if (SS::smem(true) <= IB200_STFT_SMEM_BUDGET)
+      return 2; // with per-thread twiddle rows
+    if (SS::smem(false) <= IB200_STFT_SMEM_BUDGET)
+      return 1;
+    return 0;
+  }
+}
+
+template <typename T, int L, int SH>
+cudaError_t run_stft_ws_sh(const LaunchDesc &d, int num_sms, cudaStream_t stream,
+                           int64_t *launches) {
+  using SS = StftWsShape<T, L>;
+  constexpr bool TWS = stft_ws_mode<T, L>() == 2;
+  auto kern = stft_ws_kernel<T, L, SH, TWS>;
+  const size_t smem = SS::smem(TWS);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+      return e;
+    attr = true;
+  }
+  SpecArgs<T> a = make_args<T>(d, nullptr);
+  // units of nsub consecutive tiles per CTA (one CTA per SM), as in
+  // run_stft_fast_sh
+  const int64_t tpc = (a.Tc + SS::Q - 1) / SS::Q;
+  const int64_t ctas = num_sms;
+  int nsub = (int)std::max<int64_t>(
+      1, std::min<int64_t>(32, (d.C * tpc) / std::max<int64_t>(1, 8 * ctas)));
+  const int64_t units = d.C * ((tpc + nsub - 1) / nsub);
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units, ctas));
+  kern<<<(unsigned)grid, SS::NT, smem, stream>>>(a, nsub);
+  if (launches)
+    *launches += 1;
+  return cudaGetLastError();
+}
+
 template <typename T, int L>
 cudaError_t run_stft_fast(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                           int64_t *launches) {
+  if constexpr (stft_ws_mode<T, L>() > 0) {
+    constexpr int E = values_per_thread<T>(L);
+    constexpr int R0 = Plan<L, E>::radix(0);
+    const int sh = fast_shift<T, L>(d.step);
+    if constexpr (R0 >= 4) {
+      if (sh == R0 / 4)
+        return run_stft_ws_sh<T, L, R0 / 4>(d, num_sms, stream, launches);
+    }
+    if constexpr (R0 >= 2) {
+      if (sh == R0 / 2)
+        return run_stft_ws_sh<T, L, R0 / 2>(d, num_sms, stream, launches);
+    }
+    return run_stft_ws_sh<T, L, 0>(d, num_sms, stream, launches);
+  }
   constexpr int E = values_per_thread<T>(L);
   constexpr int R0 = Plan<L, E>::radix(0);
   const int sh = fast_shift<T, L>(d.step);

@@ -27,6 +27,19 @@
 
 namespace ib200 {
 
+// Values per thread: 16 (f32) / 8 (f64) for long transforms; short
+// transforms keep at least 32 threads per group where possible.
+template <typename T> __host__ __device__ constexpr int values_per_thread(int L) {
+  const int big = std::is_same<T, float>::value ? 16 : 8;
+  const int minE = 2;
+  int e = L / 32;
+  if (e > big)
+    e = big;
+  if (e < minE)
+    e = minE;
+  return e;
+}
+
 // csd / coherence pair consecutive segments of one signal per transform and
 // stage the x and y spectra side by side, except where two spectra do not
 // fit in shared memory (f64, L = 8192): there a task is one segment and
