@@ -232,15 +232,19 @@ cudaError_t run_stft_fast_sh(const LaunchDesc &d, int num_sms,
 #ifndef IB200_STFT_WS
 #define IB200_STFT_WS 1
 #endif
+#ifndef IB200_STFT_WS_TWM
+#define IB200_STFT_WS_TWM 1
+#endif
+// 0: not usable; else 1 + the twiddle mode of the warp-specialised kernel
+// (IB200_STFT_WS_TWM or less, whichever fits the shared-memory budget)
 template <typename T, int L> constexpr int stft_ws_mode() {
   using SS = StftWsShape<T, L>;
   if constexpr (!IB200_STFT_WS || !SS::ok) {
     return 0;
   } else {
-    if (SS::smem(true) <= IB200_STFT_SMEM_BUDGET)
-      return 2; // with per-thread twiddle rows
-    if (SS::smem(false) <= IB200_STFT_SMEM_BUDGET)
-      return 1;
+    for (int twm = IB200_STFT_WS_TWM; twm >= 0; --twm)
+      if (SS::smem(twm) <= IB200_STFT_SMEM_BUDGET)
+        return 1 + twm;
     return 0;
   }
 }
@@ -249,9 +253,9 @@ template <typename T, int L, int SH>
 cudaError_t run_stft_ws_sh(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                            int64_t *launches) {
   using SS = StftWsShape<T, L>;
-  constexpr bool TWS = stft_ws_mode<T, L>() == 2;
-  auto kern = stft_ws_kernel<T, L, SH, TWS>;
-  const size_t smem = SS::smem(TWS);
+  constexpr int TWM = stft_ws_mode<T, L>() - 1;
+  auto kern = stft_ws_kernel<T, L, SH, TWM>;
+  const size_t smem = SS::smem(TWM);
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(
@@ -373,6 +377,9 @@ constexpr size_t acc_fast_smem(int G, int twm, bool stg, int mode) {
 // MAXT: threads per CTA (coherence keeps three accumulators per bin and uses
 // at most 256 threads, i.e. up to 255 registers each).  csd and coherence
 // are never shaped for f64 L = 8192 (two spectra do not fit; see packs_xy).
+#ifndef IB200_ACC_TWM
+#define IB200_ACC_TWM 2
+#endif
 template <typename T, int L, bool STG, int MODE>
 constexpr AccShape acc_fast_shape() {
   constexpr int MAXT = MODE == ACC_COH ? 256 : 512;
@@ -387,7 +394,7 @@ constexpr AccShape acc_fast_shape() {
   while (g > 1 && (g & (g - 1)) != 0)
     --g;
   for (; g >= 1; g /= 2)
-    for (int twm = 2; twm >= 0; --twm)
+    for (int twm = IB200_ACC_TWM; twm >= 0; --twm)
       if (acc_fast_smem<T, L>(g, twm, STG, MODE) <= budget)
         return {g, twm};
   return {0, 0};

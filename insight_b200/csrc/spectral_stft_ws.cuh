@@ -53,19 +53,25 @@ template <typename T, int L> struct StftWsShape {
   static constexpr bool ok = GF >= 2 && P % 32 == 0 && SPR >= SEC &&
                              SPR % SEC == 0 && NST % SPR == 0 &&
                              (NST / SPR) % SEC == 0 && GF + 5 <= 16;
-  static constexpr size_t smem(bool tws) {
+  // twm: 2 full per-thread twiddle rows, 1 first-twiddle rows (powers by
+  // multiplication: less shared-memory traffic, more FMA work), 0 table
+  __host__ __device__ static constexpr int tw_stride(int twm) {
+    return twm == 2 ? ThreadTw<T, L, E>::stride()
+                    : (twm == 1 ? ThreadTw1<T, L, E>::stride() : 0);
+  }
+  __host__ __device__ static constexpr size_t smem(int twm) {
     return (size_t)2 * Q * GS * 2 * sizeof(T) +
-           (tws ? (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T) : 0) +
+           (size_t)P * tw_stride(twm) * 2 * sizeof(T) +
            (size_t)CN * 2 * sizeof(T) + (size_t)P * WS * sizeof(T);
   }
 };
 
-template <typename T, int L, int SH, bool TWS>
+template <typename T, int L, int SH, int TWM>
 __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
     stft_ws_kernel(const SpecArgs<T> p, int nsub) {
   using V = typename V2T<T>::type;
   using SS = StftWsShape<T, L>;
-  using TT = ThreadTw<T, L, SS::E>;
+  constexpr int TWROW = SS::tw_stride(TWM);
   constexpr int E = SS::E, P = SS::P, GF = SS::GF, NFT = SS::NFT, NT = SS::NT;
   constexpr int Q = SS::Q, SPR = SS::SPR, SEC = SS::SEC, GS = SS::GS;
   constexpr int FH = SS::FH, CN = SS::CN, WS = SS::WS;
@@ -78,16 +84,18 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
   static_assert(SH >= 0 && SH < R0, "overlap shift");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   V *stage = reinterpret_cast<V *>(smem_raw);              // [2][Q][GS]
-  V *tws = stage + 2 * Q * GS;                              // [P][stride]
-  V *carry = tws + (TWS ? P * TT::stride() : 0);            // [FH][SEC-1]
+  V *tws = stage + 2 * Q * GS;                              // [P][TWROW]
+  V *carry = tws + P * TWROW;                               // [FH][SEC-1]
   T *wsm = reinterpret_cast<T *>(carry + CN);                // [P][WS]
 
   for (int i = threadIdx.x; i < P * E; i += NT) {
     const int tt = i / E, e = i - tt * E;
     wsm[tt * WS + e] = T(0.5) * p.win[in_index<L, E, P>(tt, e)];
   }
-  if constexpr (TWS)
+  if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+  else if constexpr (TWM == 1)
+    fill_thread_w1<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   __syncthreads();
 
   const int64_t tpc = (p.Tc + Q - 1) / Q;      // tiles per channel
@@ -99,7 +107,7 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
     // ------------------------------------------------------------ transforms
     const int g = threadIdx.x / P;
     const int t = threadIdx.x - g * P;
-    const V *row = tws + t * TT::stride();
+    const V *row = tws + t * TWROW;
     int64_t tile = 0; // tiles of this CTA so far (buffer = tile & 1)
     for (int64_t unit = blockIdx.x; unit < nunits; unit += gridDim.x) {
       const int64_t c = unit / upc;
@@ -151,8 +159,10 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
             }
             v[0][e] = {ra[e] * w, bv * w};
           });
-          if constexpr (TWS)
+          if constexpr (TWM == 2)
             fft_group_tw_m<T, L, E, P, GF, 1>(v, buf, GS, t, g, row);
+          else if constexpr (TWM == 1)
+            fft_group_w1<T, L, E, P, GF>(v[0], buf, t, g, row);
           else
             fft_group<T, L, E, P, GF>(v[0], buf, t, g, p.tw);
           if (p.dc_mode == 1 && t == 0)

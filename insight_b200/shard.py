@@ -60,7 +60,8 @@ def _gpu_partial(x_span, y_span, *, op, fs, window, nperseg, noverlap, nfft,
                               nperseg=nperseg, noverlap=noverlap, nfft=nfft,
                               detrend=detrend, return_onesided=return_onesided,
                               scaling=scaling, seg_range=(0, n_seg_local),
-                              raw_sums=True, stream=stream, axes=False)
+                              raw_sums=True, stream=stream, axes=False,
+                              sync=stream is None)
     return sums
 
 
