@@ -112,9 +112,11 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   __syncthreads();
   const V *row = tws + t * TWROW;
 
-  // welch keeps the window values in registers; csd and coherence (more
-  // accumulators) reread them from the shared-memory row per load.
-  constexpr int NW = MODE == ACC_PSD ? E : 1;
+  // welch keeps the window values in registers when they are few (f32 and
+  // short f64 rows); csd, coherence and long f64 rows reread them from the
+  // shared-memory row per load.
+  constexpr bool WREG = MODE == ACC_PSD && E * sizeof(T) <= 64;
+  constexpr int NW = WREG ? E : 1;
   T wreg[NW];
   static_for<0, NW>([&](auto eIC) {
     constexpr int e = decltype(eIC)::value;
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
     T wv[E];
     static_for<0, E>([&](auto eIC) {
       constexpr int e = decltype(eIC)::value;
-      if constexpr (MODE == ACC_PSD)
+      if constexpr (WREG)
         wv[e] = wreg[e];
       else
         wv[e] = wrow[e];
