@@ -30,7 +30,7 @@ namespace ib200 {
 // Values per thread: 16 (f32) / 8 (f64) for long transforms; short
 // transforms keep at least 32 threads per group where possible.
 #ifndef IB200_F64_E16_FROM
-#define IB200_F64_E16_FROM 4096
+#define IB200_F64_E16_FROM 2048
 #endif
 template <typename T> __host__ __device__ constexpr int values_per_thread(int L) {
   const int big = std::is_same<T, float>::value || L >= (IB200_F64_E16_FROM) ? 16 : 8;
