@@ -104,12 +104,16 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
               scaling, mode, axis, seg_range, raw_sums)
     xa = _abi.as_array(x)
     ya = _abi.as_array(y) if y is not None else None
-    C, S, F = spectral_shape(op, x, nperseg, noverlap, nfft, return_onesided, axis)
-    if op == _abi.OP_STFT:
-        F = (int(nfft or nperseg)) // 2 + 1
+    if out is None or axes:
+        # geometry is needed only to allocate outputs (a caller-provided out
+        # with axes=False skips this host call on the launch path)
+        C, S, F = spectral_shape(op, x, nperseg, noverlap, nfft, return_onesided,
+                                 axis)
+        if op == _abi.OP_STFT:
+            F = (int(nfft or nperseg)) // 2 + 1
+        s0, s1 = (seg_range if seg_range is not None else (0, S))
+        Sl = s1 - s0
     batched = x.ndim == 2
-    s0, s1 = (seg_range if seg_range is not None else (0, S))
-    Sl = s1 - s0
     f32 = str(x.dtype).endswith("float32")
     cdt = "complex64" if f32 else "complex128"
     if out is None:

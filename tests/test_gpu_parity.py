@@ -389,6 +389,27 @@ def test_stft(cuda, dtype, nperseg, noverlap):
     assert so.max_rel_err(got, z) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("L", [1024, 2048, 4096])
+@pytest.mark.parametrize("segments", [1, 2, 3, 9, 17, 64])
+def test_stft_complex_segment_counts(cuda, dtype, L, segments):
+    """The warp-specialised stft kernel at tile and unit edges: segment
+    counts that leave idle transform groups, a single segment, odd counts,
+    and a batch whose channels start at different sector phases."""
+    import torch
+    C, H = 5, L // 4
+    N = L + (segments - 1) * H + (segments % 3)   # a few samples to spare
+    X = np.stack([_sig(N, dtype, 40 + c) for c in range(C)])
+    f, t, z = ib.spectral(ib.OP_STFT, _to_gpu(X, cuda), nperseg=L,
+                          noverlap=L - H, complex_output=True)
+    z = _np(z)
+    assert z.shape == (C, L // 2 + 1, segments)
+    for c in range(C):
+        _, _, zr = so.stft(X[c], nperseg=L, noverlap=L - H, complex_output=True)
+        assert so.max_rel_err(z[c], zr) <= TOL[dtype]
+    torch.cuda.synchronize()
+
+
 # ------------------------------------------------------ batched / strides ----
 @pytest.mark.parametrize("layout", ["rows", "transposed_view", "interleaved"])
 def test_batched_layouts(cuda, layout):
