@@ -226,10 +226,20 @@ def reference_sample(w):
     import numpy as np
     rng = np.random.default_rng(2000)
     n = {"stft": 1 << 19, "welch": 1 << 20, "welch_f64": 1 << 18,
-         "csd": 1 << 18, "coherence": 1 << 18, "welch_long": 1 << 21}[w["name"]]
+         "csd": 1 << 18, "coherence": 1 << 18, "welch_long": 1 << 21,
+         "istft": 1 << 18}[w["name"]]
     x = rng.standard_normal(n)
     y = 0.7 * np.roll(x, 17) + 0.3 * rng.standard_normal(n)
     return x, y, n
+
+
+def sample_units(w, n):
+    """Samples one reference call on an n-sample sample accounts for."""
+    if w["op"] in ("csd", "coherence"):
+        return 2 * n
+    if w["op"] == "istft":  # output samples of the inverse
+        return ((n - w["L"]) // w["H"]) * w["H"] + w["L"]
+    return n
 
 
 def reference_call(w, x, y):
@@ -237,10 +247,18 @@ def reference_call(w, x, y):
     from oracle import ref_runner
     cores = os.cpu_count() or 1
     L, H = w["L"], w["H"]
+    if w["op"] == "istft":
+        from oracle import spectral_oracle as so
+        _, _, z = so.stft(x.astype("float32"), fs=w["fs"], window=w["window"],
+                    nperseg=L, noverlap=L - H, complex_output=True)
     if ref_runner.available():
         kind = "reference"
         cores = ref_runner.set_threads(cores)
-        if w["op"] == "stft":
+        if w["op"] == "istft":
+            fn = lambda: ref_runner.istft(z, fs=w["fs"], window=w["window"],
+                                          nperseg=L, noverlap=L - H)
+            note = "reference ins::signal::istft of a one-sided complex STFT"
+        elif w["op"] == "stft":
             xs = x.astype("float32")
             fn = lambda: ref_runner.stft(xs, fs=w["fs"], window=w["window"],
                                          nperseg=L, noverlap=L - H)
@@ -262,7 +280,10 @@ def reference_call(w, x, y):
     else:
         from oracle import spectral_oracle as so
         kind, cores = "port", 1
-        if w["op"] == "stft":
+        if w["op"] == "istft":
+            fn = lambda: so.istft(z, fs=w["fs"], window=w["window"], nperseg=L,
+                                  noverlap=L - H)
+        elif w["op"] == "stft":
             fn = lambda: so.stft(x, fs=w["fs"], window=w["window"], nperseg=L,
                                  noverlap=L - H, complex_output=True)
         elif w["op"] == "csd":
@@ -289,7 +310,7 @@ def cpu_baseline(w, min_s=10.0):
         el = time.perf_counter() - t0
         if el >= min_s or k >= 100:
             break
-    per = n * (2 if w["op"] in ("csd", "coherence") else 1)
+    per = sample_units(w, n)
     gsps = k * per / el / 1e9
     seg = (n - w["L"]) // w["H"] + 1
     desc = (f"{note}, FFT by a substitute DFT for the absent FFTW3; one channel "
@@ -313,7 +334,7 @@ def run_reference(args, w):
     for _ in range(args.steps):
         fn()
     el = time.perf_counter() - t0
-    per = n * (2 if w["op"] in ("csd", "coherence") else 1)
+    per = sample_units(w, n)
     v = args.steps * per / el / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "GSamples/s",

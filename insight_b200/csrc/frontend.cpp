@@ -786,8 +786,8 @@ C_Status run_istft(const IstftCall &c) {
           table(st, "win64|" + k, w64));
     }
     d.tw = twiddles(st, g.nfft, true);
-    ensure(st.frames, (size_t)g.C * g.S * g.nperseg * 8);
-    d.frames = reinterpret_cast<double *>(st.frames.p);
+    ensure(st.frames, (size_t)g.C * g.S * g.nperseg * (g.f64 ? 8 : 4));
+    d.frames = st.frames.p;
     // output: the caller's GPU array, or a device buffer copied back
     d.o_ss = out->strides[out->ndim - 1];
     d.o_cs = out->ndim == 2 ? out->strides[0] : 0;

@@ -77,7 +77,7 @@ struct IstftDesc {
   const void *win = nullptr;    // [nperseg] window (f64: the transform dtype)
   const double *win64 = nullptr; // [nperseg] window, f64 (normalisation)
   const void *tw = nullptr;     // [nfft] f64 twiddles
-  double *frames = nullptr;     // scratch [C][S][nperseg]
+  void *frames = nullptr;       // scratch [C][S][nperseg], input precision
   double *out = nullptr;        // element (c, m) at out[c*o_cs + m*o_ss]
   int64_t o_cs = 0, o_ss = 1;
 };

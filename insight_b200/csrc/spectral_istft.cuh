@@ -15,7 +15,10 @@
 // IFFT(Z) = a + i b.  The inverse runs on the forward kernels:
 // IFFT(Z) = conj(FFT(conj Z)) / nfft.  Other inputs (n_freq != nfft/2 + 1)
 // take one frame per task and Re(IFFT(Z)) of the zero-padded / truncated
-// column.  Windowed frames go to an f64 frame buffer [C][S][nperseg].
+// column.  Windowed frames go to a frame buffer [C][S][nperseg] in the
+// input's precision (f32 for complex64).  istft_ws_kernel is the same
+// computation for frame pairs with unit frame stride, fed by coalesced row
+// reads.
 // The transforms run in f64 for complex64 input too: the overlap-add divides
 // by the summed squared window, which is tiny where the window ends, so an
 // f32 transform's rounding would be amplified there far above 1e-5.
@@ -38,10 +41,10 @@ template <typename T, typename TZ> struct IstftArgs {
   int64_t Tc;            // tasks per channel
   const T *win;          // [nperseg] window in T
   const V *tw;           // [L] W_L^m
-  double *frames;        // [C][S][nperseg]
+  void *frames;          // [C][S][nperseg] of TF (f32 for complex64 input)
 };
 
-template <typename T, typename TZ, int L, int E, int G>
+template <typename T, typename TZ, typename TF, int L, int E, int G>
 __global__ void __launch_bounds__(G *(L / E))
     istft_frames_kernel(const IstftArgs<T, TZ> p) {
   using V = typename V2T<T>::type;
@@ -93,55 +96,326 @@ __global__ void __launch_bounds__(G *(L / E))
       v[e] = zc;
     });
     fft_group<T, L, E, P, G>(v, buf, t, g, p.tw);
-    double *fa = p.frames + (c * p.S + ia) * p.nperseg;
+    TF *fa = static_cast<TF *>(p.frames) + (c * p.S + ia) * p.nperseg;
     static_for<0, E>([&](auto eIC) {
       constexpr int e = decltype(eIC)::value;
       const int n = out_bin<L, E, P>(t, e);
       if (n < p.nperseg) {
         const T w = p.win[n];
-        fa[n] = (double)(v[e].x * inv * w);
+        fa[n] = (TF)(v[e].x * inv * w);
         if (hasb)
-          fa[p.nperseg + n] = (double)(-v[e].y * inv * w);
+          fa[p.nperseg + n] = (TF)(-v[e].y * inv * w);
       }
     });
   }
 }
 
+// Warp-specialised frame kernel for Hermitian frame pairs with unit frame
+// stride.  The frames of a tile (Q pairs, 2Q consecutive columns of every
+// bin row) are read by NLD loader threads as row runs of 2Q values (64 bytes
+// or more) with asynchronous copies (cp.async, no registers held) into one
+// of two staging buffers, [pair][bin] with the two frames of a pair side by
+// side; GF transform groups take the pairs of a full buffer (PPG each), so
+// the loads of tile n+1 are in flight while tile n is transformed.  The
+// roles meet at named barriers FULL(b) / EMPTY(b) as in stft_ws_kernel.
+template <typename TZ, int L, int E_> struct IstftWsShape {
+  static constexpr int E = E_; // f64 transforms, E values per thread
+  static constexpr int P = L / E;
+  static constexpr int NLD = 64;
+  // transform threads: up to 512 at E = 8; at E = 16 (about 128 registers a
+  // thread) the whole CTA stays within 512 threads
+  static constexpr int NFTMAX = E == 16 ? 512 - NLD : 512;
+  static constexpr int GF = (NFTMAX / P < 8 ? NFTMAX / P : 8);
+  static constexpr int NFT = GF * P;
+  static constexpr int NT = NFT + NLD;
+  static constexpr int ZB = 2 * (int)sizeof(TZ); // bytes of one input value
+  // pairs per tile: row runs of at least 48 bytes
+  static constexpr int GF1 = GF > 0 ? GF : 1;
+  static constexpr int PPG =
+      2 * GF1 * ZB >= 48 ? 1 : (64 + 2 * GF1 * ZB - 1) / (2 * GF1 * ZB);
+  static constexpr int Q = GF * PPG;
+  static constexpr int FH = L / 2 + 1;
+  // pair stride in (frame a, frame b) entries: = 2 mod 8 keeps the loaders'
+  // 8- or 16-byte writes of a row run on distinct banks
+  static constexpr int FHS = (FH + 5) / 8 * 8 + 2;
+  static constexpr int GS = spad_size(L);
+  // per-thread first-twiddle rows of the passes after the first
+  static constexpr int TWS = ThreadTw1<double, L, E>::stride();
+  static constexpr size_t smem0 = (size_t)GF * GS * 16 +
+                                  (size_t)2 * Q * FHS * 2 * ZB +
+                                  (size_t)P * TWS * 16;
+  // the f64 window in shared memory too where it fits (the opt-in maximum
+  // of a CTA is 227 KB), else read through the L1 cache
+  static constexpr bool WSM = smem0 + (size_t)L * 8 <= 232448;
+  static constexpr size_t smem = smem0 + (WSM ? (size_t)L * 8 : 0);
+  static constexpr bool ok = GF >= 2 && P % 32 == 0 && GF + 5 <= 16 &&
+                             NLD >= 2 * Q && smem0 <= 225280;
+};
+
+template <typename TZ, typename TF, int L, int E_>
+__global__ void __launch_bounds__(IstftWsShape<TZ, L, E_>::NT)
+    istft_ws_kernel(const IstftArgs<double, TZ> p) {
+  using T = double;
+  using V = double2;
+  using VZ = typename V2T<TZ>::type;
+  using SS = IstftWsShape<TZ, L, E_>;
+  constexpr int E = SS::E, P = SS::P, GF = SS::GF, NFT = SS::NFT, NT = SS::NT;
+  constexpr int NLD = SS::NLD, Q = SS::Q, PPG = SS::PPG, FH = SS::FH;
+  constexpr int FHS = SS::FHS, GS = SS::GS;
+  constexpr int FULL0 = GF + 1, EMPTY0 = GF + 3;
+  static_assert(SS::ok, "shape");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  V *scratch = reinterpret_cast<V *>(smem_raw);                // [GF][GS]
+  VZ *stage = reinterpret_cast<VZ *>(scratch + GF * GS);       // [2][Q][FHS][2]
+  V *tws = reinterpret_cast<V *>(stage + 2 * Q * FHS * 2);     // [P][TWS]
+  T *wsm = reinterpret_cast<T *>(tws + P * SS::TWS);            // [nperseg]
+  fill_thread_w1<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+  if constexpr (SS::WSM)
+    for (int i = threadIdx.x; i < p.nperseg; i += NT)
+      wsm[i] = p.win[i];
+  __syncthreads();
+  const int64_t tpc = (p.Tc + Q - 1) / Q;
+  const int64_t ntiles = p.C * tpc;
+  const int64_t mine = ntiles > blockIdx.x
+                           ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x
+                           : 0; // tiles of this CTA
+
+  if (threadIdx.x >= NFT) {
+    // ---------------------------------------------------------------- loads
+    constexpr int CPR = 2 * Q;         // columns per row run
+    constexpr int RPW = NLD / CPR;     // rows per loader round
+    const int lt = threadIdx.x - NFT;
+    const int col = lt % CPR;
+    const int kr0 = lt / CPR;
+    const int kend = lt < RPW * CPR ? FH : 0; // spare loader threads copy nothing
+    for (int64_t n = 0; n < mine; ++n) {
+      const int64_t tile = blockIdx.x + n * gridDim.x;
+      const int b = (int)(n & 1);
+      const int64_t c = tile / tpc;
+      const int64_t f = (tile - c * tpc) * (2 * Q) + col; // frame of this column
+      const bool valid = f < p.S;
+      const VZ *src = p.z + c * p.z_cs + (valid ? f : 0);
+      VZ *dst = stage + ((size_t)(b * Q + (col >> 1)) * FHS) * 2 + (col & 1);
+      if (n >= 2)
+        named_sync(EMPTY0 + b, NT); // the transforms released buffer b
+      for (int k = kr0; k < kend; k += RPW) {
+        const unsigned d =
+            static_cast<unsigned>(__cvta_generic_to_shared(dst + 2 * k));
+        const VZ *sk = src + k * p.z_fs;
+        if constexpr (sizeof(VZ) == 16)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d),
+                       "l"(sk), "r"(valid ? 16 : 0)
+                       : "memory");
+        else
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d),
+                       "l"(sk), "r"(valid ? 8 : 0)
+                       : "memory");
+      }
+      cp_async_commit();
+      if (n >= 1) {
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        named_arrive(FULL0 + (b ^ 1), NT); // tile n-1 has landed
+      }
+    }
+    if (mine >= 1) {
+      cp_async_wait_all();
+      named_arrive(FULL0 + (int)((mine - 1) & 1), NT);
+    }
+    // wait for the last releases so every barrier phase completes
+    for (int64_t k = mine >= 2 ? mine - 2 : 0; k < mine; ++k)
+      named_sync(EMPTY0 + (int)(k & 1), NT);
+    return;
+  }
+
+  // ------------------------------------------------------------ transforms
+  const int g = threadIdx.x / P;
+  const int t = threadIdx.x - g * P;
+  V *buf = scratch + g * GS;
+  const T inv = T(1) / T(L);
+  for (int64_t n = 0; n < mine; ++n) {
+    const int64_t tile = blockIdx.x + n * gridDim.x;
+    const int b = (int)(n & 1);
+    const int64_t c = tile / tpc;
+    named_sync(FULL0 + b, NT); // the loaders filled buffer b
+#pragma unroll 1
+    for (int pp = 0; pp < PPG; ++pp) {
+      const int q = g * PPG + pp;
+      const int64_t task = (tile - c * tpc) * Q + q;
+      const bool act = task < p.Tc; // uniform over the group
+      const int64_t ia = 2 * task;
+      const bool hasb = ia + 1 < p.S;
+      V v[E];
+      if (act) {
+        const VZ *ent = stage + ((size_t)(b * Q + q) * FHS) * 2;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          const int k = in_index<L, E, P>(t, e);
+          const bool mirror = k > L / 2;
+          const int kk = mirror ? L - k : k;
+          const VZ za = ent[2 * kk], zb = ent[2 * kk + 1];
+          V a{(T)za.x, (T)za.y}, bb{(T)zb.x, (T)zb.y};
+          if (kk == 0 || kk == L / 2) {
+            a.y = T(0);
+            bb.y = T(0);
+          }
+          if (mirror) {
+            a.y = -a.y;
+            bb.y = -bb.y;
+          }
+          v[e] = V{a.x - bb.y, -(a.y + bb.x)}; // conj(A + iB)
+        });
+      }
+      if (pp == PPG - 1)
+        named_arrive(EMPTY0 + b, NT); // this thread is done with buffer b
+      if (act) {
+        fft_group_w1<T, L, E, P, GF>(v, buf, t, g, tws + t * SS::TWS);
+        TF *fa = static_cast<TF *>(p.frames) + (c * p.S + ia) * p.nperseg;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          const int nn = out_bin<L, E, P>(t, e);
+          if (nn < p.nperseg) {
+            const T w = SS::WSM ? wsm[nn] : __ldg(p.win + nn);
+            fa[nn] = (TF)(v[e].x * inv * w);
+            if (hasb)
+              fa[p.nperseg + nn] = (TF)(-v[e].y * inv * w);
+          }
+        });
+      }
+    }
+  }
+}
+
 // out[c, m] = sum_i frames[c, i, m - i*hop] / sum_i w[m - i*hop]^2 over the
 // frames i covering m (unchanged where the squared-window sum is <= 1e-10).
-__global__ void istft_ola_kernel(const double *__restrict__ frames, int64_t C,
-                                 int64_t S, int64_t nperseg, int64_t hop,
-                                 int64_t n_total, const double *__restrict__ win,
-                                 double *out, int64_t o_cs, int64_t o_ss) {
-  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (idx >= C * n_total)
-    return;
-  const int64_t c = idx / n_total, m = idx - c * n_total;
-  int64_t i0 = m - nperseg + 1 <= 0 ? 0 : (m - nperseg + hop) / hop;
-  int64_t i1 = m / hop;
-  if (i1 > S - 1)
-    i1 = S - 1;
-  double s = 0.0, nrm = 0.0;
-  for (int64_t i = i0; i <= i1; ++i) {
-    const int64_t n = m - i * hop;
-    const double w = win[n];
-    s += frames[(c * S + i) * nperseg + n];
-    nrm += w * w;
+// With m = q*hop + r the covering frames are i = q - back(r) .. q, clipped
+// to 0 .. S-1, where back(r) = (nperseg-1-r)/hop; both sums run in frame
+// order.  A CTA takes channel blockIdx.y and NQ consecutive q; its threads
+// take VEC consecutive offsets r each (one 16-byte load per frame when hop
+// and nperseg are multiples of VEC, which also makes back() the same for
+// the VEC offsets), so every frame read and output write is a contiguous
+// run, and the squared-window sums of the unclipped case are formed once.
+template <typename TF, int VEC> struct alignas(sizeof(TF) * VEC) FrameVec {
+  TF v[VEC];
+};
+
+template <typename TF, int VEC>
+__global__ void __launch_bounds__(256)
+    istft_ola_kernel(const TF *__restrict__ frames, int64_t C, int64_t S,
+                     int64_t nperseg, int64_t hop, int64_t n_total,
+                     const double *__restrict__ win, double *__restrict__ out,
+                     int64_t o_cs, int64_t o_ss, int64_t nq) {
+  using FV = FrameVec<TF, VEC>;
+  const int64_t nqt = (n_total + hop - 1) / hop;
+  const int64_t q0 = blockIdx.x * nq;
+  const int64_t q1 = q0 + nq < nqt ? q0 + nq : nqt;
+  for (int64_t c = blockIdx.y; c < C; c += gridDim.y) {
+    const TF *fc = frames + c * S * nperseg;
+    double *oc = out + c * o_cs;
+    for (int r = threadIdx.x * VEC; r < hop; r += blockDim.x * VEC) {
+      const int back = (int)((nperseg - 1 - r) / hop);
+      double nrm_full[VEC];
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) {
+        nrm_full[u] = 0.0;
+        for (int j = back; j >= 0; --j) {
+          const double w = win[r + u + j * hop];
+          nrm_full[u] += w * w;
+        }
+      }
+      for (int64_t q = q0; q < q1; ++q) {
+        const int64_t m = q * hop + r;
+        if (m >= n_total)
+          break;
+        const int64_t i0 = q - back > 0 ? q - back : 0;
+        const int64_t i1 = q < S - 1 ? q : S - 1;
+        const bool clipped = i0 != q - back || i1 != q;
+        const TF *f = fc + i0 * nperseg + (m - i0 * hop);
+        const int64_t nf = i1 - i0 + 1;
+        double sum[VEC];
+#pragma unroll
+        for (int u = 0; u < VEC; ++u)
+          sum[u] = 0.0;
+        constexpr int KM = VEC > 1 ? 4 : 8; // frames loaded at once
+        if (nf <= KM) {
+          // all loads first, then the frame-order sums
+          FV fv[KM];
+#pragma unroll
+          for (int j = 0; j < KM; ++j)
+            if (j < nf)
+              fv[j] = *reinterpret_cast<const FV *>(f + j * (nperseg - hop));
+#pragma unroll
+          for (int j = 0; j < KM; ++j)
+            if (j < nf) {
+#pragma unroll
+              for (int u = 0; u < VEC; ++u)
+                sum[u] += (double)fv[j].v[u];
+            }
+        } else {
+          for (int64_t i = i0; i <= i1; ++i, f += nperseg - hop) {
+            const FV x = *reinterpret_cast<const FV *>(f);
+#pragma unroll
+            for (int u = 0; u < VEC; ++u)
+              sum[u] += (double)x.v[u];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) {
+          double nrm = nrm_full[u];
+          if (clipped) {
+            nrm = 0.0;
+            for (int64_t i = i0; i <= i1; ++i) {
+              const double w = win[m + u - i * hop];
+              nrm += w * w;
+            }
+          }
+          double v = sum[u];
+          if (fabs(nrm) > 1e-10)
+            v /= nrm;
+          oc[(m + u) * o_ss] = v;
+        }
+      }
+    }
   }
-  if (fabs(nrm) > 1e-10)
-    s /= nrm;
-  out[c * o_cs + m * o_ss] = s;
 }
+
+// Frames are kept in the input's precision: a complex64 spectrum's frames
+// (computed in f64) are rounded once to f32, a relative error that the
+// overlap-add's division by the squared-window sum does not amplify.
+template <typename TZ> using FrameT = TZ;
+
+template <typename TZ, int L, int E>
+cudaError_t run_istft_ws(const IstftArgs<double, TZ> &a, int num_sms,
+                         cudaStream_t stream) {
+  using SS = IstftWsShape<TZ, L, E>;
+  auto kern = istft_ws_kernel<TZ, FrameT<TZ>, L, E>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SS::smem);
+    if (e != cudaSuccess)
+      return e;
+    attr = true;
+  }
+  const int64_t tiles = a.C * ((a.Tc + SS::Q - 1) / SS::Q);
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms));
+  kern<<<(unsigned)grid, SS::NT, SS::smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+#ifndef IB200_ISTFT_WS
+#define IB200_ISTFT_WS 1
+#endif
 
 template <typename T, typename TZ, int L>
 cudaError_t run_istft_len(const IstftDesc &d, int num_sms, cudaStream_t stream,
                           int64_t *launches) {
   using V = typename V2T<T>::type;
   using VZ = typename V2T<TZ>::type;
+  using TF = FrameT<TZ>;
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
   constexpr int G = (P >= 32 && P <= 256) ? 256 / P : 1;
-  auto kern = istft_frames_kernel<T, TZ, L, E, G>;
+  auto kern = istft_frames_kernel<T, TZ, TF, L, E, G>;
   const size_t smem = (size_t)G * spad_size(L) * sizeof(V);
   static bool attr = false;
   if (!attr) {
@@ -165,18 +439,48 @@ cudaError_t run_istft_len(const IstftDesc &d, int num_sms, cudaStream_t stream,
   a.win = reinterpret_cast<const T *>(d.win);
   a.tw = reinterpret_cast<const V *>(d.tw);
   a.frames = d.frames;
-  const int64_t tiles = d.C * ((a.Tc + G - 1) / G);
-  const int64_t grid = std::max<int64_t>(
-      1, std::min<int64_t>(tiles, (int64_t)num_sms * 8));
-  kern<<<(unsigned)grid, G * P, smem, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  bool ws = false;
+  // the transforms' own width (16 values a thread from length 2048) where
+  // that shape fits, else 8 values a thread
+  constexpr int EW = IstftWsShape<TZ, L, E>::ok ? E : 8;
+  if constexpr (std::is_same<T, double>::value &&
+                IstftWsShape<TZ, L, EW>::ok && IB200_ISTFT_WS) {
+    // unit frame stride and an element-aligned base: cp.async row runs
+    ws = d.pack && d.z_ts == 1 &&
+         reinterpret_cast<uintptr_t>(d.z) % sizeof(VZ) == 0;
+    if (ws)
+      e = run_istft_ws<TZ, L, EW>(a, num_sms, stream);
+  }
+  if (!ws) {
+    const int64_t tiles = d.C * ((a.Tc + G - 1) / G);
+    const int64_t grid = std::max<int64_t>(
+        1, std::min<int64_t>(tiles, (int64_t)num_sms * 8));
+    kern<<<(unsigned)grid, G * P, smem, stream>>>(a);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess)
     return e;
-  const int64_t n = d.C * d.n_total;
-  const int threads = 256;
-  istft_ola_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0,
-                     stream>>>(d.frames, d.C, d.S, d.nperseg, d.hop, d.n_total,
-                               d.win64, d.out, d.o_cs, d.o_ss);
+  // threads over the offsets within a hop (VEC each), NQ hops per CTA
+  // (about 8K outputs), channels on grid.y
+  constexpr int VEC = 16 / (int)sizeof(TF);
+  const bool vec = d.hop % VEC == 0 && d.nperseg % VEC == 0;
+  const int per = vec ? VEC : 1;
+  const int threads =
+      (int)std::min<int64_t>(256, (d.hop / per + 31) / 32 * 32);
+  const int64_t nqt = (d.n_total + d.hop - 1) / d.hop;
+  const int64_t nq = std::max<int64_t>(1, 8192 / d.hop);
+  const dim3 ogrid((unsigned)((nqt + nq - 1) / nq),
+                   (unsigned)std::min<int64_t>(d.C, 65535));
+  const TF *fr = static_cast<const TF *>(d.frames);
+  if (vec)
+    istft_ola_kernel<TF, VEC><<<ogrid, threads, 0, stream>>>(
+        fr, d.C, d.S, d.nperseg, d.hop, d.n_total, d.win64, d.out, d.o_cs,
+        d.o_ss, nq);
+  else
+    istft_ola_kernel<TF, 1><<<ogrid, threads, 0, stream>>>(
+        fr, d.C, d.S, d.nperseg, d.hop, d.n_total, d.win64, d.out, d.o_cs,
+        d.o_ss, nq);
   if (launches)
     *launches += 2;
   return cudaGetLastError();

@@ -292,6 +292,26 @@ def test_istft(cuda, cdtype, L, stft_ov, nperseg, noverlap, nfft, window):
     assert err <= (1e-5 if cdtype == np.complex64 else 1e-12), err
 
 
+@pytest.mark.parametrize("cdtype", [np.complex64, np.complex128])
+@pytest.mark.parametrize("L,hop,S", [(2048, 512, 1501), (2048, 512, 1000),
+                                     (1024, 256, 777), (512, 128, 2048)])
+def test_istft_many_frames(cuda, cdtype, L, hop, S):
+    """Hundreds of frame pairs per CTA, odd and even frame counts: the
+    pipelined frame kernel's tile sequence, its last partial tile and the
+    overlap-add's interior and clipped edges."""
+    import torch
+    x = _sig((S - 1) * hop + L, np.float64, 31)
+    _, _, z = so.stft(x, nperseg=L, noverlap=L - hop, complex_output=True)
+    z = z.astype(cdtype)
+    assert z.shape[1] == S
+    got = _np(ib.istft(torch.from_numpy(np.ascontiguousarray(z)).to(cuda),
+                       nperseg=L, noverlap=L - hop))
+    ref = so.istft(z, nperseg=L, noverlap=L - hop)
+    assert got.shape == ref.shape
+    err = _istft_err(got, ref, S, L, hop, "hann")
+    assert err <= (1e-5 if cdtype == np.complex64 else 1e-12), err
+
+
 @pytest.mark.parametrize("layout", ["batch", "strided_view", "host", "two_sided"])
 def test_istft_layouts(cuda, layout):
     import torch
