@@ -398,7 +398,24 @@ template <typename T, int L, int E> struct ThreadTw1 {
   __host__ __device__ static constexpr int stride() { return total() | 1; }
 };
 
-template <typename T, int L, int E, int P, typename V>
+// Mirrored butterfly assignment of the last pass.  Butterfly j of the last
+// pass (radix R, NS = L/R) yields bins j + NS*r, whose mirrors L - bin are
+// the bins of butterfly NS - j (element R-1-r), or of j itself for j = 0
+// and j = NS/2.  With B = E/R >= 2 butterflies per thread, thread t takes
+// j = t + b*P for b < B/2 and the mirror of each for b >= B/2 (NS/2 in place
+// of the mirror of 0), so it holds both Z[k] and Z[L-k] of all its bins.
+template <int L, int E, int P>
+__host__ __device__ constexpr int pair_j(int t, int b) {
+  using PL = Plan<L, E>;
+  constexpr int R = PL::radix(PL::passes() - 1);
+  constexpr int NS = L / R, H = E / R / 2;
+  if (b < H)
+    return t + b * P;
+  const int j = t + (b - H) * P;
+  return j == 0 ? NS / 2 : NS - j;
+}
+
+template <typename T, int L, int E, int P, typename V, bool PAIRS = false>
 __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
                                                int nthreads) {
   using PL = Plan<L, E>;
@@ -414,7 +431,9 @@ __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
       constexpr int NS = PL::ns(p);
       if (slot >= TT::offset(p) && slot < TT::offset(p + 1)) {
         const int b = slot - TT::offset(p);
-        const int k = (tt + b * P) & (NS - 1);
+        const int j =
+            (PAIRS && p == NPASS - 1) ? pair_j<L, E, P>(tt, b) : tt + b * P;
+        const int k = j & (NS - 1);
         val = tw[k * (L / (NS * R))];
       }
     });
@@ -446,6 +465,45 @@ __device__ __forceinline__ void fft_group_w1(V *v, V *buf, int t, int g,
     constexpr int p = decltype(pIC)::value;
     if constexpr (p > 0) {
       pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+    pass_compute_w1<T, L, E, P, p>(v, row1);
+    if constexpr (p + 1 < NP) {
+      pass_store<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+  });
+}
+
+// fft_group_w1 whose last pass runs the mirrored butterflies of pair_j (the
+// rows must come from fill_thread_w1<..., true>).  The transform is left in
+// registers: element r of butterfly b, bin pair_j(t, b) + r*L/R, at
+// v[b*R + bitrev(r)].
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group_w1_pairs(V *v, V *buf, int t, int g,
+                                                   const V *row1) {
+  using PL = Plan<L, E>;
+  constexpr int NP = PL::passes();
+  constexpr int RL = PL::radix(NP - 1);
+  constexpr int BL = E / RL;
+  static_assert(NP >= 2 && BL >= 2, "mirrored pairs need two butterflies");
+  static_for<0, NP>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0 && p + 1 < NP) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    } else if constexpr (p > 0) {
+      static_for<0, BL>([&](auto bIC) {
+        constexpr int b = decltype(bIC)::value;
+        const int j = pair_j<L, E, P>(t, b);
+        static_for<0, RL>([&](auto rIC) {
+          constexpr int r = decltype(rIC)::value;
+          if constexpr ((L / RL) % 16 == 0)
+            v[b * RL + r] = buf[spad(j) + pad_off<r * (L / RL)>()];
+          else
+            v[b * RL + r] = buf[spad(j + r * (L / RL))];
+        });
+      });
       group_sync<G, P>(g);
     }
     pass_compute_w1<T, L, E, P, p>(v, row1);

@@ -67,6 +67,22 @@ __device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
 // the first twiddle of each butterfly (1), or from full per-thread rows (2).
 // Coherence CTAs (256 threads) are register-capped at 128 so that two fit
 // on an SM next to each other.
+// MIR (csd, coherence with first-twiddle rows): the last pass runs on
+// mirrored butterflies (pair_j), so every thread holds Z[k] and Z[L-k] of
+// its bins in registers; x's transform is parked in the thread's own column
+// of its buffer while y is transformed, and the cross products need no
+// staged spectra, no shared-memory gathers of Z[k], Z[L-k] and one group
+// barrier fewer per task.
+#ifndef IB200_ACC_MIR
+#define IB200_ACC_MIR 1
+#endif
+template <typename T, int L, int E>
+__host__ __device__ constexpr bool acc_mirrored(int mode, int twm) {
+  return IB200_ACC_MIR && mode != ACC_PSD && twm == 1 &&
+         Plan<L, E>::passes() >= 2 &&
+         E / Plan<L, E>::radix(Plan<L, E>::passes() - 1) >= 2;
+}
+
 template <typename T, int L, int E, int G, int SH, int TWM, int MODE, bool STG>
 __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
     accum_fast_kernel(const SpecArgs<T> p) {
@@ -84,6 +100,11 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   constexpr int FL = sizeof(T) == 4 ? 16 : 1; // transforms per f32 partial
   constexpr int NF = MODE == ACC_PSD ? NACC : 1; // f32 partial accumulators
   static_assert(SH >= 0 && SH < R0, "overlap shift");
+  constexpr bool MIR = acc_mirrored<T, L, E>(MODE, TWM);
+  constexpr int RL = PL::radix(PL::passes() - 1); // last-pass radix
+  constexpr int NSL = L / RL;
+  constexpr int HB = E / RL / 2; // mirrored butterfly pairs per thread
+  static_assert(!MIR || NB == E / 2 + 1, "mirrored bins: E/2 + Nyquist");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // welch: one transform buffer and a 2L staging span per group; csd and
   // coherence: x and y buffers, x and y staging spans.
@@ -108,9 +129,18 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   else if constexpr (TWM == 1)
-    fill_thread_w1<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
+    fill_thread_w1<T, L, E, P, V, MIR>(tws, p.tw, threadIdx.x, NT);
   __syncthreads();
   const V *row = tws + t * TWROW;
+  // MIR: bin of accumulator slot s (s < E/2: butterfly pair h = s / RL,
+  // element r = (s % RL) / 2, the mirror half when s is odd; slot E/2 is the
+  // Nyquist bin of thread 0)
+  auto mir_bin = [&](int s) -> int {
+    if (s == E / 2)
+      return L / 2;
+    const int h = s / RL, r = (s % RL) / 2;
+    return pair_j<L, E, P>(t, h + (s & 1) * HB) + NSL * r;
+  };
 
   // welch keeps the window values in registers when they are few (f32 and
   // short f64 rows); csd, coherence and long f64 rows reread them from the
@@ -166,7 +196,9 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
     }
   };
   auto fft = [&](V(&v)[E], V *b) {
-    if constexpr (TWM == 2)
+    if constexpr (MIR)
+      fft_group_w1_pairs<T, L, E, P, G>(v, b, t, g, row);
+    else if constexpr (TWM == 2)
       fft_group_tw_m<T, L, E, P, G, 1>(&v, b, GS, t, g, row);
     else if constexpr (TWM == 1)
       fft_group_w1<T, L, E, P, G>(v, b, t, g, row);
@@ -242,6 +274,64 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
 #pragma unroll
         for (int e = 0; e < E; ++e)
           accf[e] = fma(v[e].x, v[e].x, fma(v[e].y, v[e].y, accf[e]));
+      } else if constexpr (MIR) {
+        fft(v, buf);
+        // park x's registers in this thread's column of buf: every read of
+        // buf by the transform ended at its last group barrier
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          buf[e * P + t] = v[e];
+        load_v(v, STG ? raw + 2 * L + t : yc + off + t, boff, hasb);
+        if constexpr (STG) {
+          group_sync<G, P>(g); // the staging spans are free again
+          if (task + G < task1)
+            issue(task + G);
+        }
+        fft(v, buf2);
+        // Zx = Xa + i Xb, Zy = Ya + i Yb: as in the staged epilogue below,
+        // from registers (y) and the parked column (x)
+        auto bin = [&](auto sIC, V xk, V xm, V yk, V ym) {
+          constexpr int s = decltype(sIC)::value;
+          const T xar = xk.x + xm.x, xai = xk.y - xm.y;
+          const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
+          const T yar = yk.x + ym.x, yai = yk.y - ym.y;
+          const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
+          const T re = fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
+          if constexpr (MODE == ACC_COH) {
+            acc[3 * s] +=
+                (double)fma(xar, xar, fma(xai, xai, fma(xbr, xbr, xbi * xbi)));
+            acc[3 * s + 1] +=
+                (double)fma(yar, yar, fma(yai, yai, fma(ybr, ybr, ybi * ybi)));
+            acc[3 * s + 2] += (double)re;
+          } else {
+            const T im = fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+            acc[2 * s] += (double)re;
+            acc[2 * s + 1] += (double)im;
+          }
+        };
+        auto px = [&](int e) { return buf[e * P + t]; };
+        const bool j0 = t == 0; // butterflies 0 and NS/2 mirror themselves
+        static_for<0, HB>([&](auto hIC) {
+          constexpr int h = decltype(hIC)::value;
+          static_for<0, RL / 2>([&](auto rIC) {
+            constexpr int r = decltype(rIC)::value;
+            constexpr int ea = h * RL + bitrev<RL>(r);
+            constexpr int eam = (h + HB) * RL + bitrev<RL>(RL - 1 - r);
+            constexpr int eself = h * RL + bitrev<RL>((RL - r) % RL);
+            constexpr int ec = (h + HB) * RL + bitrev<RL>(r);
+            constexpr int ecm = h * RL + bitrev<RL>(RL - 1 - r);
+            const bool self = h == 0 && j0;
+            bin(std::integral_constant<int, h * RL + 2 * r>{}, px(ea),
+                px(self ? eself : eam), v[ea], self ? v[eself] : v[eam]);
+            bin(std::integral_constant<int, h * RL + 2 * r + 1>{}, px(ec),
+                px(self ? eam : ecm), v[ec], self ? v[eam] : v[ecm]);
+          });
+        });
+        if (j0) {
+          constexpr int en = bitrev<RL>(RL / 2);
+          bin(std::integral_constant<int, E / 2>{}, px(en), px(en), v[en], v[en]);
+        }
+        group_sync<G, P>(g); // the parked column is read before buf is reused
       } else {
         fft(v, buf);
         store_bins<L, E, P>(v, buf, t);
@@ -328,7 +418,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
         double2 *sm = reinterpret_cast<double2 *>(buf);
 #pragma unroll
         for (int i = 0; i < NB; ++i) {
-          const int k = t + i * P;
+          const int k = MIR ? (i < E / 2 || t == 0 ? mir_bin(i) : FH) : t + i * P;
           if (k < FH) {
             if constexpr (r == 0)
               sm[k] = make_double2(acc[W * i], acc[W * i + 1]);

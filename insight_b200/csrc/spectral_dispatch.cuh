@@ -393,8 +393,11 @@ constexpr AccShape acc_fast_shape() {
     g = 1;
   while (g > 1 && (g & (g - 1)) != 0)
     --g;
+  // csd / coherence: first-twiddle rows, for the mirrored last pass
+  constexpr int TW0 =
+      acc_mirrored<T, L, E>(MODE, 1) ? 1 : IB200_ACC_TWM;
   for (; g >= 1; g /= 2)
-    for (int twm = IB200_ACC_TWM; twm >= 0; --twm)
+    for (int twm = TW0; twm >= 0; --twm)
       if (acc_fast_smem<T, L>(g, twm, STG, MODE) <= budget)
         return {g, twm};
   return {0, 0};
