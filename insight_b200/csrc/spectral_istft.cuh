@@ -129,10 +129,10 @@ template <typename TZ, int L, int E_> struct IstftWsShape {
   static constexpr int NFT = GF * P;
   static constexpr int NT = NFT + NLD;
   static constexpr int ZB = 2 * (int)sizeof(TZ); // bytes of one input value
-  // pairs per tile: row runs of at least 48 bytes
+  // pairs per tile: row runs of at least 32 bytes
   static constexpr int GF1 = GF > 0 ? GF : 1;
   static constexpr int PPG =
-      2 * GF1 * ZB >= 48 ? 1 : (64 + 2 * GF1 * ZB - 1) / (2 * GF1 * ZB);
+      2 * GF1 * ZB >= 32 ? 1 : (64 + 2 * GF1 * ZB - 1) / (2 * GF1 * ZB);
   static constexpr int Q = GF * PPG;
   static constexpr int FH = L / 2 + 1;
   // pair stride in (frame a, frame b) entries: = 2 mod 8 keeps the loaders'
@@ -441,9 +441,10 @@ cudaError_t run_istft_len(const IstftDesc &d, int num_sms, cudaStream_t stream,
   a.frames = d.frames;
   cudaError_t e = cudaSuccess;
   bool ws = false;
-  // the transforms' own width (16 values a thread from length 2048) where
-  // that shape fits, else 8 values a thread
-  constexpr int EW = IstftWsShape<TZ, L, E>::ok ? E : 8;
+  // 8 values a thread where that shape fits (at length 2048: 18 warps a
+  // CTA at 96 registers and the window in shared memory, against 14 warps at
+  // 128 registers with 16 values), else the transforms' own width
+  constexpr int EW = IstftWsShape<TZ, L, 8>::ok ? 8 : E;
   if constexpr (std::is_same<T, double>::value &&
                 IstftWsShape<TZ, L, EW>::ok && IB200_ISTFT_WS) {
     // unit frame stride and an element-aligned base: cp.async row runs
