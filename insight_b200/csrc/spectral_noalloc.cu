@@ -76,7 +76,7 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
   using ib200::set_last_error;
   const cudaStream_t st = (cudaStream_t)stream;
   if (!x || !pxx) {
-    set_last_error("csd: inputs are undefined");
+    set_last_error("welch_noalloc: inputs are undefined");
     return C_FAILED;
   }
   if (dtype != INSIGHT_DTYPE_F32 && dtype != INSIGHT_DTYPE_F64) {
@@ -89,7 +89,7 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
     return C_FAILED;
   }
   if (nperseg <= 0) {
-    set_last_error("csd: nperseg must be positive");
+    set_last_error("welch_noalloc: nperseg must be positive");
     return C_FAILED;
   }
   // Defaults and framing as the reference csd (spectral_analysis.cpp:114-125).
@@ -99,18 +99,18 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
     noverlap = nperseg / 2;
   const int64_t step = nperseg - noverlap;
   if (step <= 0) {
-    set_last_error("csd: noverlap must be less than nperseg");
+    set_last_error("welch_noalloc: noverlap must be less than nperseg");
     return C_FAILED;
   }
   const int64_t S =
       (n_samples >= nperseg) ? ((n_samples - nperseg) / step + 1) : 0;
   if (S < 1) {
-    set_last_error("csd: signal too short for given nperseg");
+    set_last_error("welch_noalloc: signal too short for given nperseg");
     return C_FAILED;
   }
   if (!ib200::nfft_supported(nfft) || nfft < nperseg) {
-    set_last_error("csd: nfft must be a power of two in [16, 8192] and >= "
-                   "nperseg on the B200 backend");
+    set_last_error("welch_noalloc: nfft must be a power of two in [16, 8192] "
+                   "and >= nperseg on the B200 backend");
     return C_FAILED;
   }
   std::vector<double> w;
@@ -118,6 +118,13 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
     w = ib200::get_window(window ? window : "hann", nperseg, false);
   } catch (const std::exception &e) {
     set_last_error(e.what());
+    return C_FAILED;
+  }
+  const bool constant = detrend && std::string(detrend) == "constant";
+  if (constant && nfft != nperseg) {
+    set_last_error("welch_noalloc: detrend='constant' needs nfft == nperseg "
+                   "(zero padding with constant detrend uses a device table "
+                   "that this entry point does not hold)");
     return C_FAILED;
   }
   const bool f64 = dtype == INSIGHT_DTYPE_F64;
@@ -154,6 +161,13 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
     set_last_error(err);
     return C_FAILED;
   }
+  int num_sms = 0;
+  e = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess || num_sms < 1) {
+    set_last_error(std::string("welch_noalloc: multiprocessor count: ") +
+                   cudaGetErrorString(e));
+    return C_FAILED;
+  }
 
   // Tables on the host, copied into the scratch array on the caller's stream
   // (the copies from pageable memory have left the host buffers on return).
@@ -177,20 +191,21 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
     else
       reinterpret_cast<float *>(win.data())[i] = (float)w[i];
   }
+  // Every check that can reject the call is done above: from here on a
+  // failure first waits for what this call queued, so no copy of a failed
+  // call is still writing the shared array when the call returns.
   e = cudaMemcpyAsync(base + tw_off, tw.data(), tw.size(), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(base + win_off, win.data(), win.size(),
                         cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) {
+    cudaStreamSynchronize(st);
     set_last_error(std::string("welch_noalloc: ") + cudaGetErrorString(e));
     return C_FAILED;
   }
 
-  const bool constant = detrend && std::string(detrend) == "constant";
   const double scale =
       ((scaling && std::string(scaling) != "density") ? 1.0 : fs) / wss;
-  int num_sms = 0;
-  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
 
   ib200::LaunchDesc d;
   d.kind = ib200::LK_PSD;
@@ -207,13 +222,7 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
   d.win = base + win_off;
   d.tw = base + tw_off;
   d.dtab = nullptr;
-  d.dc_mode = !constant ? 0 : (nfft == nperseg ? 1 : 2);
-  if (d.dc_mode == 2) {
-    set_last_error("welch_noalloc: detrend='constant' needs nfft == nperseg "
-                   "(zero padding with constant detrend uses a device table "
-                   "that this entry point does not hold)");
-    return C_FAILED;
-  }
+  d.dc_mode = !constant ? 0 : 1;
   d.F = F;
   d.onesided_mask = onesided && nfft > 1;
   d.avg_scale = scale / (double)S;
@@ -224,8 +233,9 @@ insight_b200_welch_noalloc(const void *x, int32_t dtype, int64_t n_channels,
   int64_t nl = 0;
   e = ib200::launch(d, base + part_off, num_sms, st, &nl);
   ib200::add_launches(nl);
+  const cudaError_t es = cudaStreamSynchronize(st);
   if (e == cudaSuccess)
-    e = cudaStreamSynchronize(st);
+    e = es;
   if (e != cudaSuccess) {
     set_last_error(std::string("welch_noalloc: ") + cudaGetErrorString(e));
     return C_FAILED;

@@ -6,7 +6,7 @@ seeded inputs and stores inputs and outputs in tests/golden/reference_cases.npz.
 Also records the C ABI layout of the reference's headers
 (include/insight/c_api/*.h) in tests/golden/abi_layout.json.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py <reference source tree>
 
 The fixtures are committed; the tests never need the reference tree.
 """
@@ -174,4 +174,6 @@ def main(ref_tree: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference source tree>")
+    main(sys.argv[1])

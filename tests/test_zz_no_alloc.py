@@ -67,6 +67,47 @@ def test_noalloc_matches_regular_entry_point_twice(cuda):
     assert torch.isfinite(out2).all()
 
 
+def test_noalloc_near_its_limit_two_sided_and_padded(cuda):
+    """Shapes that reach the caps on the work split (1000 channels of 513
+    f64 partial-sum bins take most of the 8 MiB array), a two-sided result
+    and zero padding, each checked against the regular entry point; after a
+    warm-up call, a further call leaves the device's free memory unchanged."""
+    import torch
+    torch.cuda.set_device(cuda)
+    rng = np.random.default_rng(78)
+    C, N = 1000, 1 << 14
+    xt = torch.from_numpy(rng.standard_normal((C, N)).astype(np.float32)).to(cuda)
+    kw = dict(fs=2.0, nperseg=1024)
+    out = torch.full((C, 513), float("nan"), dtype=torch.float64, device=cuda)
+    assert _noalloc(xt, _abi.DT_F32, C, N, N, 1, out, **kw) == 0, _abi.last_error()
+    _, ref = ib.spectral(ib.OP_WELCH, xt, **kw)
+    assert so.max_rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+
+    # two-sided f32, 3 channels
+    x3 = xt[:3]
+    kw3 = dict(nperseg=512, noverlap=384, return_onesided=False)
+    out3 = torch.full((3, 512), float("nan"), dtype=torch.float64, device=cuda)
+    assert _noalloc(x3, _abi.DT_F32, 3, N, N, 1, out3, **kw3) == 0, _abi.last_error()
+    _, ref3 = ib.spectral(ib.OP_WELCH, x3, **kw3)
+    assert so.max_rel_err(out3.cpu().numpy(), ref3.cpu().numpy()) <= 1e-5
+
+    # f32 with zero padding (nfft > nperseg) and no detrend
+    kw4 = dict(nperseg=1000, nfft=2048, detrend="none", window="blackman")
+    out4 = torch.full((2, 1025), float("nan"), dtype=torch.float64, device=cuda)
+    assert _noalloc(xt, _abi.DT_F32, 2, N, N, 1, out4, **kw4) == 0, _abi.last_error()
+    _, ref4 = ib.spectral(ib.OP_WELCH, xt[:2], **kw4)
+    assert so.max_rel_err(out4.cpu().numpy(), ref4.cpu().numpy()) <= 1e-5
+
+    # no device allocation: the free bytes do not move across a call
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda)
+    assert _noalloc(xt, _abi.DT_F32, C, N, N, 1, out, **kw) == 0, _abi.last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda)
+    assert free1 == free0
+    assert so.max_rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+
+
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda):
     import torch
     x = torch.zeros((1024, 8192), dtype=torch.float64, device=cuda)
