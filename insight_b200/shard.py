@@ -83,13 +83,17 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
                           scaling: str = "density",
                           all_reduce: Optional[Callable] = None,
                           partial: Callable = _gpu_partial,
-                          finalize: Callable = _gpu_finalize, stream=None):
+                          finalize: Callable = _gpu_finalize, stream=None,
+                          on_phase: Optional[Callable[[str], None]] = None):
     """Welch PSD (or csd) of one long signal sharded by segment range.
 
     x_span (and y_span) hold this rank's samples [lo, hi) of
     segment_shard(n_samples, nperseg, noverlap, rank, world).  Returns the
     reduced, scaled result on every rank.  all_reduce(tensor) sums in place
-    over the ranks (torch.distributed.all_reduce by default).
+    over the ranks (torch.distributed.all_reduce by default).  on_phase(name),
+    when given, is called after each of the three steps has been enqueued
+    ("partial", "all_reduce", "finalize"), e.g. to record a CUDA event on
+    the stream between them.
     """
     step, S = framing(n_samples, nperseg, noverlap)
     s0, s1, lo, hi = segment_shard(n_samples, nperseg, noverlap, rank, world)
@@ -100,6 +104,8 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
               scaling=scaling)
     sums = partial(x_span, y_span if op == "csd" else None, n_seg_local=s1 - s0,
                    stream=stream, **kw)
+    if on_phase is not None:
+        on_phase("partial")
     if all_reduce is None:
         import torch.distributed as dist
         all_reduce = dist.all_reduce
@@ -111,7 +117,12 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
                 all_reduce(sums)
         else:
             all_reduce(sums)
+    if on_phase is not None:
+        on_phase("all_reduce")
     x_dtype = str(x_span.dtype)
-    return finalize(sums, op=op, n_seg=S, x_dtype=x_dtype, fs=fs, window=window,
-                    nperseg=nperseg, nfft=nfft, return_onesided=return_onesided,
-                    scaling=scaling, stream=stream)
+    res = finalize(sums, op=op, n_seg=S, x_dtype=x_dtype, fs=fs, window=window,
+                   nperseg=nperseg, nfft=nfft, return_onesided=return_onesided,
+                   scaling=scaling, stream=stream)
+    if on_phase is not None:
+        on_phase("finalize")
+    return res

@@ -22,9 +22,11 @@
 #include "insight/c_api/kernel.h"
 #include "insight/c_api/place.h"
 #include "insight/core/array.h"
+#include "insight/core/op_registry.h"
 #include "insight/init.h"
 #include "insight/ops/creation.h"
 #include "insight/ops/signal/spectral_analysis.h"
+#include "insight/ops/signal/windows.h"
 
 #include <omp.h>
 
@@ -238,6 +240,141 @@ int ref_spectrogram(const void *x, int64_t n, int dtype, double fs,
     *n_freq = copy_out(r.f, f_out, cap);
     *n_seg = copy_out(r.t, t_out, cap);
     copy_out(r.Sxx, s_out, cap);
+    return 0;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The B200 plugin reached only through the reference's own core.
+//
+// ref_load_gpu_backend: the reference's loader (src/init.cpp: load_backend ->
+// try_load_backend) finds libinsight_<name>_backend.so in search_dir, calls
+// its InitPluginGPU with the core's insight_register_kernel, installs the
+// C_DeviceInterface it fills and initialises device 0.  The calling thread's
+// default place is then set back to the CPU so the reference's CPU
+// composites above keep computing on the CPU (the core would otherwise make
+// GPUPlace(0) the default once a GPU backend is present,
+// src/core/place.cpp:252-261).
+int ref_load_gpu_backend(const char *search_dir, const char *name) {
+  try {
+    if (search_dir && search_dir[0])
+      ins::add_backend_search_path(search_dir);
+    ins::load_backend(name);
+    if (!ins::has_device(ins::DeviceKind::GPU)) {
+      g_err = std::string("the core did not load libinsight_") + name +
+              "_backend as its GPU backend";
+      return 1;
+    }
+    ins::set_device(ins::CPUPlace());
+    return 0;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
+// insight_has_kernel of the core's registry for a GPU kernel.
+int ref_has_gpu_kernel(const char *op, int dtype) {
+  return insight_has_kernel(op, INSIGHT_DEVICE_GPU, dtype);
+}
+
+namespace {
+
+// compute_psd_scale (spectral_analysis.cpp:57-67): (fs or 1) / sum(w^2), the
+// window taken in the input dtype.
+double psd_scale_of(const ins::Array &win_cpu, int dtype, double fs,
+                    const std::string &scaling) {
+  ins::Array w = win_cpu.contiguous();
+  const double *wv = w.data<double>();
+  double ss = 0.0;
+  for (int64_t i = 0; i < w.numel(); ++i) {
+    const double v = dtype == INSIGHT_DTYPE_F32 ? (double)(float)wv[i] : wv[i];
+    ss += v * v;
+  }
+  return (scaling == "density" ? fs : 1.0) / ss;
+}
+
+} // namespace
+
+// The GPU branch a maintainer adds at the top of the reference's csd / welch
+// / coherence (op = "csd", "welch" or "coherence"): inputs moved to
+// GPUPlace(0) by the core's Array::to (the plugin's device interface does
+// the allocation and the copy), the window made by the reference's own
+// get_window and moved to the GPU, the output allocated on the GPU by the
+// core, the kernel launched by ops().launch with the registry layout, and
+// the result brought back by Array::to(CPUPlace()).
+int ref_gpu_csd(const char *op, const void *x, const void *y, int64_t n,
+                int dtype, double fs, const char *window, int64_t nperseg,
+                int64_t noverlap, int64_t nfft, const char *detrend,
+                int onesided, const char *scaling, double *f_out,
+                double *p_out, int64_t cap, int64_t *n_freq) {
+  try {
+    const ins::Place gpu = ins::GPUPlace(0);
+    ins::Array xg = make_input(x, n, dtype).to(gpu);
+    ins::Array yg = y ? make_input(y, n, dtype).to(gpu) : xg;
+    if (nfft == 0)
+      nfft = nperseg;
+    if (noverlap == 0)
+      noverlap = nperseg / 2;
+    ins::Array win = ins::signal::get_window(window, nperseg, false);
+    const double scale = psd_scale_of(win.to(ins::CPUPlace()), dtype, fs, scaling);
+    ins::Array wg = win.to(gpu);
+    const int64_t F = onesided ? nfft / 2 + 1 : nfft;
+    ins::Array P(ins::Shape({F}), ins::DType::F64, gpu); // every bin is written
+    int32_t dcode = std::string(detrend) == "constant" ? 1 : 0;
+    int32_t os = onesided ? 1 : 0;
+    double sc = scale;
+    int64_t axis = -1;
+    ins::ops().launch(op, gpu, xg.dtype(),
+                      {P.layout_ptr(), xg.layout_ptr(), yg.layout_ptr(),
+                       wg.layout_ptr(), &nperseg, &noverlap, &nfft, &dcode, &os,
+                       &sc, &axis},
+                      {P.layout_ptr()});
+    *n_freq = F;
+    for (int64_t i = 0; i < F && i < cap; ++i)
+      f_out[i] = (double)i * (fs / (double)nfft);
+    copy_out(P, p_out, cap);
+    return 0;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
+// The GPU branch of the reference's stft (spectrogram with mode complex,
+// detrend none, one-sided): the (n_freq, n_seg) F64 buffer of Re(X) that the
+// reference builds before its transposed view, written by the registered
+// "stft" kernel and returned as that (n_freq, n_seg) row-major buffer.
+int ref_gpu_stft(const void *x, int64_t n, int dtype, double fs,
+                 const char *window, int64_t nperseg, int64_t noverlap,
+                 int64_t nfft, double *s_out, int64_t cap, int64_t *n_seg,
+                 int64_t *n_freq) {
+  try {
+    const ins::Place gpu = ins::GPUPlace(0);
+    ins::Array xg = make_input(x, n, dtype).to(gpu);
+    if (nfft == 0)
+      nfft = nperseg;
+    if (noverlap == 0)
+      noverlap = nperseg / 8;
+    const int64_t step = nperseg - noverlap;
+    const int64_t S = n >= nperseg ? (n - nperseg) / step + 1 : 0;
+    const int64_t F = nfft / 2 + 1;
+    ins::Array wg = ins::signal::get_window(window, nperseg, false).to(gpu);
+    ins::Array out(ins::Shape({F, S}), ins::DType::F64, gpu); // fully written
+    int32_t dcode = 0, os = 1, mode = 1;
+    double sc = 1.0;
+    int64_t axis = -1;
+    ins::ops().launch("stft", gpu, xg.dtype(),
+                      {out.layout_ptr(), xg.layout_ptr(), wg.layout_ptr(),
+                       &nperseg, &noverlap, &nfft, &dcode, &os, &mode, &sc,
+                       &axis},
+                      {out.layout_ptr()});
+    *n_seg = S;
+    *n_freq = F;
+    copy_out(out, s_out, cap);
     return 0;
   } catch (const std::exception &e) {
     g_err = e.what();

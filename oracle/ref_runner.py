@@ -3,7 +3,7 @@
 Test infrastructure only: runs the reference's own ins::signal::welch / csd /
 spectrogram / stft (src/ops/signal/spectral_analysis.cpp) through
 oracle/ref_harness.cpp.  The reference's CPU "fft" kernel exists only with
-FFTW3, which is absent here; the harness registers a substitute DFT kernel
+FFTW3, which is absent here; the harness registers a substitute FFT kernel
 through the reference's insight_register_kernel C ABI (see ref_harness.cpp).
 """
 from __future__ import annotations
@@ -176,3 +176,76 @@ def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0,
 
 def stft(x, fs=1.0, window="hann", nperseg=256, noverlap=0, nfft=0):
     return spectrogram(x, fs, window, nperseg, noverlap, nfft, is_stft=True)
+
+
+# ---------------------------------------------------------------------------
+# The B200 plugin through the reference's own core (loader, registry, Array).
+# ---------------------------------------------------------------------------
+def load_gpu_backend(search_dir: str, name: str = "b200") -> None:
+    """ins::load_backend(name) with search_dir added to the core's backend
+    search paths: the core dlopens libinsight_<name>_backend.so, calls its
+    InitPluginGPU and installs its device interface.  Raises with the core's
+    message when the plugin is not accepted."""
+    L = lib()
+    L.ref_load_gpu_backend.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+    if L.ref_load_gpu_backend(search_dir.encode(), name.encode()) != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+
+
+def has_gpu_kernel(op: str, dtype_code: int) -> bool:
+    """insight_has_kernel(op, GPU, dtype) of the core's registry."""
+    L = lib()
+    L.ref_has_gpu_kernel.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    return bool(L.ref_has_gpu_kernel(op.encode(), dtype_code))
+
+
+def gpu_csd(op, x, y=None, fs=1.0, window="hann", nperseg=256, noverlap=0,
+            nfft=0, detrend="constant", return_onesided=True, scaling="density"):
+    """The frontend's GPU branch of csd / welch / coherence run by the core:
+    inputs moved to GPUPlace(0) by Array::to, output allocated by the core,
+    the registered kernel launched by ops().launch.  Returns (f, P)."""
+    L = lib()
+    x = np.ascontiguousarray(x)
+    if y is not None:
+        y = np.ascontiguousarray(y, dtype=x.dtype)
+    I = ctypes.c_int64
+    P = ctypes.POINTER(ctypes.c_double)
+    L.ref_gpu_csd.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p, I,
+                              ctypes.c_int, ctypes.c_double, ctypes.c_char_p, I, I,
+                              I, ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p, P,
+                              P, I, ctypes.POINTER(I)]
+    cap = (nfft or nperseg) + 2
+    f = np.zeros(cap)
+    p = np.zeros(cap)
+    nf = I()
+    rc = L.ref_gpu_csd(op.encode(), x.ctypes.data, None if y is None else y.ctypes.data,
+                       len(x), _dt(x), fs, window.encode(), nperseg, noverlap, nfft,
+                       detrend.encode(), 1 if return_onesided else 0,
+                       scaling.encode(), f.ctypes.data_as(P), p.ctypes.data_as(P),
+                       cap, ctypes.byref(nf))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    return f[:nf.value].copy(), p[:nf.value].copy()
+
+
+def gpu_stft(x, window="hann", nperseg=256, noverlap=0, nfft=0):
+    """The frontend's GPU branch of stft run by the core: Re(X) as the
+    (n_freq, n_seg) F64 buffer the reference builds, written by the
+    registered "stft" kernel."""
+    L = lib()
+    x = np.ascontiguousarray(x)
+    I = ctypes.c_int64
+    P = ctypes.POINTER(ctypes.c_double)
+    L.ref_gpu_stft.argtypes = [ctypes.c_void_p, I, ctypes.c_int, ctypes.c_double,
+                               ctypes.c_char_p, I, I, I, P, I, ctypes.POINTER(I),
+                               ctypes.POINTER(I)]
+    _, S0 = framing(len(x), nperseg, noverlap, for_spectrogram=True)
+    F0 = (nfft or nperseg) // 2 + 1
+    s = np.zeros(max(S0 * F0, 1))
+    ns, nf = I(), I()
+    rc = L.ref_gpu_stft(x.ctypes.data, len(x), _dt(x), 1.0, window.encode(), nperseg,
+                        noverlap, nfft, s.ctypes.data_as(P), s.size, ctypes.byref(ns),
+                        ctypes.byref(nf))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    return s[:nf.value * ns.value].reshape(nf.value, ns.value).copy()

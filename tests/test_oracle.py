@@ -147,3 +147,38 @@ def test_reference_f32_welch_throws_as_documented():
         pytest.skip("oracle/_ref not built")
     with pytest.raises(RuntimeError, match="item<float64>"):
         ref_runner.welch(np.zeros(1024, np.float32), nperseg=256)
+
+
+# ------------------------------------------- configuration-scale fixtures --
+import sys as _sys  # noqa: E402
+
+_sys.path.insert(0, GOLDEN)
+import config_inputs as _ci  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def config_golden():
+    return np.load(os.path.join(GOLDEN, "reference_configs.npz"))
+
+
+@pytest.mark.parametrize("case", _ci.CASES, ids=lambda c: c[0])
+def test_oracle_matches_reference_at_config_parameters(case, config_golden):
+    """The restatement against the reference's own outputs at the benchmark
+    configurations' nperseg, windows, overlaps and detrend (one channel or
+    pair each, inputs promoted to F64 as the reference needs)."""
+    name, make, op, kw = case
+    g = config_golden
+    if op == "csd":
+        x, y = make()
+        f, p = so.csd(x.astype(np.float64), y.astype(np.float64), **kw)
+    elif op == "welch":
+        f, p = so.welch(make().astype(np.float64), **kw)
+    else:
+        f, t, s = so.stft(make().astype(np.float64), **kw)
+        assert np.array_equal(t, g[name + "/t"])
+        expect = so.reference_spectrogram_layout(s, "complex", kw["nperseg"])
+        assert np.array_equal(f, g[name + "/f"])
+        assert so.max_rel_err(expect, g[name + "/Sxx"]) <= 1e-12
+        return
+    assert np.array_equal(f, g[name + "/f"])
+    assert so.max_rel_err(p, g[name + "/Pxx"]) <= 1e-12
