@@ -70,6 +70,26 @@ struct DevBuf {
   size_t n = 0;
 };
 
+// A constant table: device copy, the host bytes it was copied from (kept so
+// the asynchronous upload never reads freed memory) and an event recorded
+// after the upload on the stream that made it; users on any stream wait for
+// that event instead of synchronising the host.
+struct Table {
+  DevBuf buf;
+  std::vector<unsigned char> host;
+  cudaEvent_t ready = nullptr;
+};
+
+// Working buffers a launch reads and writes on the device (welch/csd partial
+// sums, istft frames), one set per stream: calls on different streams never
+// share them, so asynchronous calls on two streams can run at the same time.
+// `last` is recorded after each use; a later use waits for it, which keeps a
+// set correct even if its stream handle is reused by a new stream.
+struct StreamBufs {
+  DevBuf scratch, frames;
+  cudaEvent_t last = nullptr;
+};
+
 struct DeviceState {
   int dev = 0;
   int num_sms = 0;
@@ -81,8 +101,11 @@ struct DeviceState {
   cudaStream_t pipe[kPipe] = {};
   cudaEvent_t pipe_start = nullptr;
   std::mutex mu;
-  DevBuf scratch, xin, yin, out, win_tmp, frames;
-  std::map<std::string, DevBuf> tables;
+  // staging of host inputs / outputs: used only by calls that synchronise
+  // their stream before returning
+  DevBuf xin, yin, out, win_tmp;
+  std::map<cudaStream_t, StreamBufs> per_stream;
+  std::map<std::string, Table> tables;
 };
 
 std::mutex g_states_mu;
@@ -111,17 +134,35 @@ DeviceState &device_state(int dev) {
   return *slot;
 }
 
-void ensure(DevBuf &b, size_t bytes) {
+// Grow-only buffer, stream-ordered: the old block is released and the new
+// one taken on `stream` (cudaFreeAsync / cudaMallocAsync), after the work
+// already queued there, without synchronising the device.
+void ensure(DevBuf &b, size_t bytes, cudaStream_t stream) {
   if (b.n >= bytes && b.p)
     return;
   if (b.p) {
-    cuda_check(cudaFree(b.p), "cudaFree");
+    cuda_check(cudaFreeAsync(b.p, stream), "cudaFreeAsync");
     b.p = nullptr;
     b.n = 0;
   }
   size_t n = std::max<size_t>(bytes, 256);
-  cuda_check(cudaMalloc(&b.p, n), "cudaMalloc");
+  cuda_check(cudaMallocAsync(&b.p, n, stream), "cudaMallocAsync");
   b.n = n;
+}
+
+// The per-stream working buffers of `stream`, ordered after their last use.
+StreamBufs &stream_bufs(DeviceState &st, cudaStream_t stream) {
+  StreamBufs &sb = st.per_stream[stream];
+  if (!sb.last)
+    cuda_check(cudaEventCreateWithFlags(&sb.last, cudaEventDisableTiming),
+               "cudaEventCreate");
+  else
+    cuda_check(cudaStreamWaitEvent(stream, sb.last, 0), "cudaStreamWaitEvent");
+  return sb;
+}
+
+void mark_used(StreamBufs &sb, cudaStream_t stream) {
+  cuda_check(cudaEventRecord(sb.last, stream), "cudaEventRecord");
 }
 
 size_t dtype_size(int32_t dt) {
@@ -146,21 +187,30 @@ std::vector<unsigned char> pack_complex(const std::vector<double> &re,
   return b;
 }
 
+// Constant table `key`, uploaded on first use with an asynchronous copy on
+// the call's stream; every use makes the call's stream wait for the upload.
 const void *table(DeviceState &st, const std::string &key,
-                  const std::vector<unsigned char> &bytes) {
+                  std::vector<unsigned char> bytes, cudaStream_t stream) {
   auto it = st.tables.find(key);
-  if (it != st.tables.end())
-    return it->second.p;
-  DevBuf b;
-  ensure(b, bytes.size());
-  cuda_check(cudaMemcpy(b.p, bytes.data(), bytes.size(), cudaMemcpyHostToDevice),
-             "cudaMemcpy");
-  st.tables[key] = b;
-  return b.p;
+  if (it != st.tables.end()) {
+    cuda_check(cudaStreamWaitEvent(stream, it->second.ready, 0),
+               "cudaStreamWaitEvent");
+    return it->second.buf.p;
+  }
+  Table &t = st.tables[key];
+  t.host = std::move(bytes);
+  ensure(t.buf, t.host.size(), stream);
+  cuda_check(cudaMemcpyAsync(t.buf.p, t.host.data(), t.host.size(),
+                             cudaMemcpyHostToDevice, stream),
+             "cudaMemcpyAsync");
+  cuda_check(cudaEventCreateWithFlags(&t.ready, cudaEventDisableTiming),
+             "cudaEventCreate");
+  cuda_check(cudaEventRecord(t.ready, stream), "cudaEventRecord");
+  return t.buf.p;
 }
 
 // W_L^m = exp(-2 pi i m / L), evaluated in double.
-const void *twiddles(DeviceState &st, int64_t L, bool f64) {
+const void *twiddles(DeviceState &st, int64_t L, bool f64, cudaStream_t stream) {
   std::vector<double> re(L), im(L);
   for (int64_t m = 0; m < L; ++m) {
     const double a = 2.0 * M_PI * (double)m / (double)L;
@@ -168,12 +218,14 @@ const void *twiddles(DeviceState &st, int64_t L, bool f64) {
     im[m] = -std::sin(a);
   }
   std::string key = std::string("tw|") + (f64 ? "d|" : "f|") + std::to_string(L);
-  return table(st, key, f64 ? pack_complex<double>(re, im)
-                            : pack_complex<float>(re, im));
+  return table(st, key,
+               f64 ? pack_complex<double>(re, im) : pack_complex<float>(re, im),
+               stream);
 }
 
 // D[k] = sum_{n < M} W_L^{nk} = (1 - W^{kM}) / (1 - W^k), D[0] = M.
-const void *dc_table(DeviceState &st, int64_t L, int64_t M, bool f64) {
+const void *dc_table(DeviceState &st, int64_t L, int64_t M, bool f64,
+                     cudaStream_t stream) {
   std::vector<double> re(L), im(L);
   for (int64_t k = 0; k < L; ++k) {
     if (k == 0) {
@@ -191,8 +243,9 @@ const void *dc_table(DeviceState &st, int64_t L, int64_t M, bool f64) {
   }
   std::string key = std::string("dc|") + (f64 ? "d|" : "f|") +
                     std::to_string(L) + "|" + std::to_string(M);
-  return table(st, key, f64 ? pack_complex<double>(re, im)
-                            : pack_complex<float>(re, im));
+  return table(st, key,
+               f64 ? pack_complex<double>(re, im) : pack_complex<float>(re, im),
+               stream);
 }
 
 // Window values cast to the compute dtype and zero padded to nfft.
@@ -280,25 +333,42 @@ bool contiguous(const InsightArray *a) {
   return true;
 }
 
-// Write host F64 values into a caller array (CPU or GPU, contiguous F64).
-void put_host_vector(const std::vector<double> &v, InsightArray *dst,
-                     const char *what, cudaStream_t stream) {
+// The f (F values) or t (S values) axis array of a call: checked, and the
+// address of element 0 (nullptr when the caller passed none).
+double *axis_array(InsightArray *dst, int64_t n, const char *what, int dev) {
   if (!dst)
-    return;
+    return nullptr;
   check(dst->dtype == INSIGHT_DTYPE_F64,
         std::string(what) + " must be an F64 array");
-  check(numel(dst) == (int64_t)v.size(),
-        std::string(what) + " has " + std::to_string(numel(dst)) +
-            " elements, expected " + std::to_string(v.size()));
+  check(numel(dst) == n, std::string(what) + " has " + std::to_string(numel(dst)) +
+                             " elements, expected " + std::to_string(n));
   check(contiguous(dst), std::string(what) + " must be contiguous");
-  char *p = reinterpret_cast<char *>(dst->data) + dst->offset * 8;
-  if (dst->device_type == INSIGHT_DEVICE_GPU) {
-    cuda_check(cudaMemcpyAsync(p, v.data(), v.size() * 8, cudaMemcpyHostToDevice,
-                               stream),
-               "cudaMemcpyAsync");
-    cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
-  } else {
-    std::memcpy(p, v.data(), v.size() * 8);
+  check(dst->device_type != INSIGHT_DEVICE_GPU || dst->device_id == dev,
+        std::string(what) + " on a different device");
+  return reinterpret_cast<double *>(dst->data) + dst->offset;
+}
+
+// f[i] = i * (fs / nfft) and t[i] = (i * step + nperseg / 2) / fs
+// (spectral_analysis.cpp:47-55, :250-253): host arrays are filled here, GPU
+// arrays by a kernel on the call's stream with the same double operations
+// (bit-identical values, no host buffer and no synchronisation).
+void write_axes(const std::vector<double> &fvec, const std::vector<double> &tvec,
+                InsightArray *f, InsightArray *t, double df, int64_t step,
+                double half, double fs, int dev, cudaStream_t stream) {
+  double *fp = axis_array(f, (int64_t)fvec.size(), "f", dev);
+  double *tp = axis_array(t, (int64_t)tvec.size(), "t", dev);
+  const bool fg = fp && f->device_type == INSIGHT_DEVICE_GPU;
+  const bool tg = tp && t->device_type == INSIGHT_DEVICE_GPU;
+  if (fp && !fg)
+    std::memcpy(fp, fvec.data(), fvec.size() * 8);
+  if (tp && !tg)
+    std::memcpy(tp, tvec.data(), tvec.size() * 8);
+  if (fg || tg) {
+    cuda_check(write_axes_device(fg ? fp : nullptr, (int64_t)fvec.size(), df,
+                                 tg ? tp : nullptr, (int64_t)tvec.size(), step,
+                                 half, fs, stream),
+               "axes kernel");
+    g_launches += 1;
   }
 }
 
@@ -412,7 +482,7 @@ C_Status run(const Call &c) {
         check(v.dev == dev, std::string(op) + ": inputs on different devices");
         return base_ptr(v.a);
       }
-      ensure(buf, v.span * es);
+      ensure(buf, v.span * es, stream);
       cuda_check(cudaMemcpyAsync(buf.p, base_ptr(v.a), v.span * es,
                                  cudaMemcpyHostToDevice, stream),
                  "cudaMemcpyAsync");
@@ -425,30 +495,32 @@ C_Status run(const Call &c) {
                            c.out->device_type != INSIGHT_DEVICE_GPU &&
                            xv.C >= 2 && xv.cs >= (xv.N - 1) * xv.ss + 1;
     if (host_pipe) {
-      ensure(st.xin, xv.span * dtype_size(xv.dtype));
+      ensure(st.xin, xv.span * dtype_size(xv.dtype), stream);
       d.x = st.xin.p;
     } else {
       d.x = stage(xv, st.xin);
     }
     d.y = two ? stage(yv, st.yin) : nullptr;
 
-    // Tables.
+    // Tables.  Caller window values (registry kernels) are copied from `wb`,
+    // which lives until the call returns; such calls synchronise their
+    // stream before returning (must_sync below).
+    std::vector<unsigned char> wb;
     if (c.window_values) {
-      auto wb = window_bytes(w, nfft, f64);
-      ensure(st.win_tmp, wb.size());
+      wb = window_bytes(w, nfft, f64);
+      ensure(st.win_tmp, wb.size(), stream);
       cuda_check(cudaMemcpyAsync(st.win_tmp.p, wb.data(), wb.size(),
                                  cudaMemcpyHostToDevice, stream),
                  "cudaMemcpyAsync");
-      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
       d.win = st.win_tmp.p;
     } else {
       std::string key = std::string("win|") + (f64 ? "d|" : "f|") + c.window +
                         "|" + std::to_string(c.nperseg) + "|" +
                         std::to_string(nfft);
-      d.win = table(st, key, window_bytes(w, nfft, f64));
+      d.win = table(st, key, window_bytes(w, nfft, f64), stream);
     }
-    d.tw = twiddles(st, nfft, f64);
-    d.dtab = dc_mode == 2 ? dc_table(st, nfft, c.nperseg, f64) : nullptr;
+    d.tw = twiddles(st, nfft, f64, stream);
+    d.dtab = dc_mode == 2 ? dc_table(st, nfft, c.nperseg, f64, stream) : nullptr;
 
     // Output array.
     InsightArray *out = c.out;
@@ -550,7 +622,7 @@ C_Status run(const Call &c) {
     if (direct) {
       obase = reinterpret_cast<char *>(out->data) + out->offset * (int64_t)oes;
     } else {
-      ensure(st.out, span * oes);
+      ensure(st.out, span * oes, stream);
       obase = st.out.p;
     }
     d.out = obase;
@@ -601,8 +673,8 @@ C_Status run(const Call &c) {
       g_launches += nl;
       for (int i = 0; i < DeviceState::kPipe; ++i)
         cuda_check(cudaStreamSynchronize(st.pipe[i]), "cudaStreamSynchronize");
-      put_host_vector(fvec, c.f, "f", stream);
-      put_host_vector(tvec, c.t, "t", stream);
+      write_axes(fvec, tvec, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
+      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
       return C_SUCCESS;
     }
     if (host_pipe) // output channels interleave: one copy of the whole input
@@ -611,13 +683,19 @@ C_Status run(const Call &c) {
                                  cudaMemcpyHostToDevice, stream),
                  "cudaMemcpyAsync");
 
-    // Scratch and launch.
+    // Scratch (this stream's own) and launch.
     const size_t sb = scratch_bytes(d, st.num_sms);
-    if (sb)
-      ensure(st.scratch, sb);
+    StreamBufs *sbuf = nullptr;
+    if (sb) {
+      sbuf = &stream_bufs(st, stream);
+      ensure(sbuf->scratch, sb, stream);
+    }
     int64_t nl = 0;
-    cuda_check(launch(d, st.scratch.p, st.num_sms, stream, &nl), "kernel launch");
+    cuda_check(launch(d, sbuf ? sbuf->scratch.p : nullptr, st.num_sms, stream, &nl),
+               "kernel launch");
     g_launches += nl;
+    if (sbuf)
+      mark_used(*sbuf, stream);
 
     if (!direct) {
       char *hp = reinterpret_cast<char *>(out->data) + out->offset * (int64_t)oes;
@@ -625,14 +703,13 @@ C_Status run(const Call &c) {
                                  stream),
                  "cudaMemcpyAsync");
     }
-    const bool must_sync = c.sync || !xv.gpu || !direct || (two && !yv.gpu);
+    write_axes(fvec, tvec, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
+    const bool must_sync = c.sync || !xv.gpu || !direct || (two && !yv.gpu) ||
+                           c.window_values != nullptr;
     if (must_sync)
       cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     else
       cuda_check(cudaGetLastError(), "kernel launch");
-
-    put_host_vector(fvec, c.f, "f", stream);
-    put_host_vector(tvec, c.t, "t", stream);
     return C_SUCCESS;
   } catch (const std::exception &e) {
     set_last_error(e.what());
@@ -754,7 +831,7 @@ C_Status run_istft(const IstftCall &c) {
       d.z = base_ptr(z);
     } else {
       const int64_t span = (g.C - 1) * g.cs + (g.F - 1) * g.fs + (g.S - 1) * g.ts + 1;
-      ensure(st.xin, span * zes);
+      ensure(st.xin, span * zes, stream);
       cuda_check(cudaMemcpyAsync(st.xin.p, base_ptr(z), span * zes,
                                  cudaMemcpyHostToDevice, stream),
                  "cudaMemcpyAsync");
@@ -763,11 +840,14 @@ C_Status run_istft(const IstftCall &c) {
     // tables: window in the compute dtype and in f64, twiddles
     std::vector<unsigned char> w64(w.size() * 8);
     std::memcpy(w64.data(), w.data(), w64.size());
-    // the transforms run in f64 for both input precisions
+    // the transforms run in f64 for both input precisions; caller window
+    // values (registry kernel) are copied from wb / w64, which live until the
+    // call returns (such calls synchronise their stream before returning)
+    std::vector<unsigned char> wb;
     if (c.window_values) {
-      auto wb = window_bytes(w, g.nperseg, true);
+      wb = window_bytes(w, g.nperseg, true);
       const size_t off = (wb.size() + 15) / 16 * 16; // f64 copy after it
-      ensure(st.win_tmp, off + w64.size());
+      ensure(st.win_tmp, off + w64.size(), stream);
       char *p = reinterpret_cast<char *>(st.win_tmp.p);
       cuda_check(cudaMemcpyAsync(p, wb.data(), wb.size(), cudaMemcpyHostToDevice,
                                  stream),
@@ -775,19 +855,19 @@ C_Status run_istft(const IstftCall &c) {
       cuda_check(cudaMemcpyAsync(p + off, w64.data(), w64.size(),
                                  cudaMemcpyHostToDevice, stream),
                  "cudaMemcpyAsync");
-      cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
       d.win = p;
       d.win64 = reinterpret_cast<const double *>(p + off);
     } else {
       const std::string k = c.window + "|" + std::to_string(g.nperseg);
       d.win = table(st, std::string("win|d|") + k + "|" + std::to_string(g.nperseg),
-                    window_bytes(w, g.nperseg, true));
+                    window_bytes(w, g.nperseg, true), stream);
       d.win64 = reinterpret_cast<const double *>(
-          table(st, "win64|" + k, w64));
+          table(st, "win64|" + k, w64, stream));
     }
-    d.tw = twiddles(st, g.nfft, true);
-    ensure(st.frames, (size_t)g.C * g.S * g.nperseg * (g.f64 ? 8 : 4));
-    d.frames = st.frames.p;
+    d.tw = twiddles(st, g.nfft, true, stream);
+    StreamBufs &sbuf = stream_bufs(st, stream);
+    ensure(sbuf.frames, (size_t)g.C * g.S * g.nperseg * (g.f64 ? 8 : 4), stream);
+    d.frames = sbuf.frames.p;
     // output: the caller's GPU array, or a device buffer copied back
     d.o_ss = out->strides[out->ndim - 1];
     d.o_cs = out->ndim == 2 ? out->strides[0] : 0;
@@ -795,18 +875,19 @@ C_Status run_istft(const IstftCall &c) {
     if (ogpu) {
       d.out = reinterpret_cast<double *>(out->data) + out->offset;
     } else {
-      ensure(st.out, ospan * 8);
+      ensure(st.out, ospan * 8, stream);
       d.out = reinterpret_cast<double *>(st.out.p);
     }
     int64_t nl = 0;
     cuda_check(launch_istft(d, st.num_sms, stream, &nl), "istft launch");
     g_launches += nl;
+    mark_used(sbuf, stream);
     if (!ogpu) {
       cuda_check(cudaMemcpyAsync(reinterpret_cast<double *>(out->data) + out->offset,
                                  d.out, ospan * 8, cudaMemcpyDeviceToHost, stream),
                  "cudaMemcpyAsync");
     }
-    if (c.sync || !zgpu || !ogpu)
+    if (c.sync || !zgpu || !ogpu || c.window_values)
       cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     else
       cuda_check(cudaGetLastError(), "istft launch");

@@ -97,6 +97,13 @@ struct AccSplit {
 };
 AccSplit acc_split(const LaunchDesc &d, int num_sms, int blocks_per_sm);
 
+// f[i] = i * df (F values) and t[i] = (i * step + half) / fs (S values) on the
+// device, bit-identical to the same double expressions on the host; a null
+// pointer skips that axis.
+cudaError_t write_axes_device(double *f, int64_t F, double df, double *t,
+                              int64_t S, int64_t step, double half, double fs,
+                              cudaStream_t stream);
+
 // sums[c, k] *= factor * (mask && 1 <= k <= F-2 ? 2 : 1); complex sums are
 // interleaved double pairs.
 cudaError_t scale_sums(double *sums, int64_t C, int64_t F, bool complex_sums,
