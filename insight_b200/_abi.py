@@ -221,20 +221,21 @@ _NP_DT = {"float32": DT_F32, "float64": DT_F64, "complex64": DT_C32,
 
 def _fill(a: InsightArray, ptr: int, shape, strides, dtype: int, dev_type: int,
           dev_id: int, offset: int = 0) -> InsightArray:
+    nd = len(shape)
+    if nd > MAX_NDIM:
+        raise ValueError(f"InsightArray holds at most {MAX_NDIM} dimensions")
     a.data = ptr
-    a.ndim = len(shape)
+    a.ndim = nd
+    a.dims[:nd] = shape
+    a.strides[:nd] = strides
     n = 1
-    for i, (d, s) in enumerate(zip(shape, strides)):
-        a.dims[i] = int(d)
-        a.strides[i] = int(s)
-        n *= int(d)
+    for d in shape:
+        n *= d
     a.numel = n
     a.dtype = dtype
     a.device_type = dev_type
     a.device_id = dev_id
     a.offset = offset
-    a.is_view = 0
-    a.ref_count = None
     return a
 
 
@@ -243,7 +244,8 @@ def from_numpy(x) -> InsightArray:
     dt = _NP_DT[str(x.dtype)]
     item = x.dtype.itemsize
     strides = [s // item for s in x.strides]
-    return _fill(InsightArray(), x.ctypes.data, x.shape, strides, dt, DEV_CPU, 0)
+    return _fill(InsightArray(), x.ctypes.data, tuple(x.shape), strides, dt,
+                 DEV_CPU, 0)
 
 
 _TORCH_DT = {"torch.float32": DT_F32, "torch.float64": DT_F64,
@@ -258,8 +260,8 @@ def from_torch(t) -> InsightArray:
     else:
         dev_type, dev_id = DEV_CPU, 0
     base = t.untyped_storage().data_ptr()
-    return _fill(InsightArray(), base, tuple(t.shape), tuple(t.stride()), dt,
-                 dev_type, dev_id, t.storage_offset())
+    return _fill(InsightArray(), base, t.shape, t.stride(), dt, dev_type, dev_id,
+                 t.storage_offset())
 
 
 def as_array(x) -> InsightArray:

@@ -352,24 +352,43 @@ double *axis_array(InsightArray *dst, int64_t n, const char *what, int dev) {
 // (spectral_analysis.cpp:47-55, :250-253): host arrays are filled here, GPU
 // arrays by a kernel on the call's stream with the same double operations
 // (bit-identical values, no host buffer and no synchronisation).
-void write_axes(const std::vector<double> &fvec, const std::vector<double> &tvec,
-                InsightArray *f, InsightArray *t, double df, int64_t step,
-                double half, double fs, int dev, cudaStream_t stream) {
-  double *fp = axis_array(f, (int64_t)fvec.size(), "f", dev);
-  double *tp = axis_array(t, (int64_t)tvec.size(), "t", dev);
+void write_axes(int64_t F, int64_t S, InsightArray *f, InsightArray *t, double df,
+                int64_t step, double half, double fs, int dev, cudaStream_t stream) {
+  double *fp = axis_array(f, F, "f", dev);
+  double *tp = axis_array(t, S, "t", dev);
   const bool fg = fp && f->device_type == INSIGHT_DEVICE_GPU;
   const bool tg = tp && t->device_type == INSIGHT_DEVICE_GPU;
   if (fp && !fg)
-    std::memcpy(fp, fvec.data(), fvec.size() * 8);
+    for (int64_t i = 0; i < F; ++i)
+      fp[i] = i * df;
   if (tp && !tg)
-    std::memcpy(tp, tvec.data(), tvec.size() * 8);
+    for (int64_t i = 0; i < S; ++i)
+      tp[i] = (i * step + half) / fs;
   if (fg || tg) {
-    cuda_check(write_axes_device(fg ? fp : nullptr, (int64_t)fvec.size(), df,
-                                 tg ? tp : nullptr, (int64_t)tvec.size(), step,
-                                 half, fs, stream),
+    cuda_check(write_axes_device(fg ? fp : nullptr, F, df, tg ? tp : nullptr, S,
+                                 step, half, fs, stream),
                "axes kernel");
     g_launches += 1;
   }
+}
+
+// Window values by (name, length), computed once per process (the table
+// uploads are cached per device below).
+const std::vector<double> &window_values_of(const std::string &name, int64_t n) {
+  static std::mutex mu;
+  static std::map<std::pair<std::string, int64_t>, std::vector<double>> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(name, n);
+  auto it = cache.find(key);
+  if (it != cache.end())
+    return it->second;
+  std::vector<double> w;
+  try {
+    w = get_window(name, n, false);
+  } catch (const std::invalid_argument &e) {
+    throw Fail(e.what());
+  }
+  return cache.emplace(key, std::move(w)).first->second;
 }
 
 } // namespace
@@ -425,18 +444,10 @@ C_Status run(const Call &c) {
           std::string(op) + ": segment range out of bounds");
 
     // Window: caller values (registry kernels) or by name.
-    std::vector<double> w;
-    if (c.window_values) {
-      w = *c.window_values;
-      check((int64_t)w.size() == c.nperseg,
-            std::string(op) + ": window must have nperseg values");
-    } else {
-      try {
-        w = get_window(c.window, c.nperseg, false);
-      } catch (const std::invalid_argument &e) {
-        throw Fail(e.what());
-      }
-    }
+    const std::vector<double> &w =
+        c.window_values ? *c.window_values : window_values_of(c.window, c.nperseg);
+    check((int64_t)w.size() == c.nperseg,
+          std::string(op) + ": window must have nperseg values");
     double scale = c.has_scale ? c.scale
                                : ((c.scaling == "density" ? c.fs : 1.0) /
                                   window_sum_sq(w, f64));
@@ -444,14 +455,8 @@ C_Status run(const Call &c) {
                         : !c.detrend_constant ? 0
                                               : (nfft == c.nperseg ? 1 : 2);
 
-    // Result geometry and output arrays.
-    std::vector<double> fvec(F);
+    // Result geometry (the f and t axes are written at the end, if asked for).
     const double df = c.fs / (double)nfft;
-    for (int64_t i = 0; i < F; ++i)
-      fvec[i] = i * df;
-    std::vector<double> tvec(S);
-    for (int64_t i = 0; i < S; ++i)
-      tvec[i] = (i * step + c.nperseg / 2.0) / c.fs;
 
     const int dev = xv.gpu ? xv.dev : c.default_device;
     cuda_check(cudaSetDevice(dev), "cudaSetDevice");
@@ -673,7 +678,7 @@ C_Status run(const Call &c) {
       g_launches += nl;
       for (int i = 0; i < DeviceState::kPipe; ++i)
         cuda_check(cudaStreamSynchronize(st.pipe[i]), "cudaStreamSynchronize");
-      write_axes(fvec, tvec, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
+      write_axes(F, S, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
       cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
       return C_SUCCESS;
     }
@@ -703,7 +708,7 @@ C_Status run(const Call &c) {
                                  stream),
                  "cudaMemcpyAsync");
     }
-    write_axes(fvec, tvec, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
+    write_axes(F, S, c.f, c.t, df, step, c.nperseg / 2.0, c.fs, dev, stream);
     const bool must_sync = c.sync || !xv.gpu || !direct || (two && !yv.gpu) ||
                            c.window_values != nullptr;
     if (must_sync)
@@ -793,17 +798,10 @@ C_Status run_istft(const IstftCall &c) {
     check(out->ndim == (z->ndim == 3 ? 2 : 1) &&
               out->dims[out->ndim - 1] == g.n_total,
           "istft: output must be [n_total] (or [C, n_total] for a batch)");
-    std::vector<double> w;
-    if (c.window_values) {
-      w = *c.window_values;
-      check((int64_t)w.size() == g.nperseg, "istft: window must have nperseg values");
-    } else {
-      try {
-        w = get_window(c.window, g.nperseg, false);
-      } catch (const std::invalid_argument &e) {
-        throw Fail(e.what());
-      }
-    }
+    const std::vector<double> &w = c.window_values
+                                       ? *c.window_values
+                                       : window_values_of(c.window, g.nperseg);
+    check((int64_t)w.size() == g.nperseg, "istft: window must have nperseg values");
     const bool zgpu = z->device_type == INSIGHT_DEVICE_GPU;
     const bool ogpu = out->device_type == INSIGHT_DEVICE_GPU;
     const int dev = zgpu ? z->device_id : (ogpu ? out->device_id : c.default_device);
@@ -932,12 +930,7 @@ C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums) {
     check(sums && sums->device_type == INSIGHT_DEVICE_GPU,
           "finalize_sums: sums must be a GPU array");
     const bool f64 = c.x_dtype == INSIGHT_DTYPE_F64;
-    std::vector<double> w;
-    try {
-      w = get_window(c.window, c.nperseg, false);
-    } catch (const std::invalid_argument &e) {
-      throw Fail(e.what());
-    }
+    const std::vector<double> &w = window_values_of(c.window, c.nperseg);
     const double scale =
         (c.scaling == "density" ? c.fs : 1.0) / window_sum_sq(w, f64);
     const int64_t nfft = c.nfft == 0 ? c.nperseg : c.nfft;

@@ -163,15 +163,12 @@ cudaError_t run_accum(const LaunchDesc &d, void *scratch, int num_sms,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return e;
-  const int64_t n = d.C * d.F;
-  const int threads = 256;
-  const int64_t blocks = (n + threads - 1) / threads;
-  spectral_finalize_kernel<MODE><<<(unsigned)blocks, threads, 0, stream>>>(
-      a.scratch, d.C, sp.nq, 0, d.nfft, d.F, d.avg_scale, d.onesided_mask ? 1 : 0,
-      d.out, d.o_cs, d.out_kind);
+  e = launch_finalize<MODE>(a.scratch, d.C, sp.nq, 0, d.nfft, d.F, d.avg_scale,
+                            d.onesided_mask ? 1 : 0, d.out, d.o_cs, d.out_kind,
+                            stream);
   if (launches)
     *launches += 2;
-  return cudaGetLastError();
+  return e;
 }
 
 // Overlap shift of the fast path: hop = SH * L/R0 with SH in {R0/4, R0/2}
@@ -445,6 +442,9 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
   const int64_t T_all = d.C * a.Tc;
   int64_t grid = std::min<int64_t>(
       T_all, (int64_t)num_sms * std::min(blocks_per_sm, kFlatMaxBlocksPerSm));
+  // small problems: at least G transforms a CTA, so no transform group idles
+  // and the finalize reads fewer partial slots
+  grid = std::min<int64_t>(grid, std::max<int64_t>(1, T_all / G));
   if (d.max_units > 0) {
     if (d.max_units < d.C)
       return cudaErrorInvalidValue;
@@ -455,15 +455,12 @@ cudaError_t run_accum_fast_sh(const LaunchDesc &d, void *scratch, int num_sms,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return e;
-  const int64_t n = d.C * d.F;
-  const int threads = 256;
-  spectral_finalize_kernel<MODE><<<(unsigned)((n + threads - 1) / threads),
-                                   threads, 0, stream>>>(
-      a.scratch, d.C, grid, T_all, d.nfft, d.F, d.avg_scale,
-      d.onesided_mask ? 1 : 0, d.out, d.o_cs, d.out_kind);
+  e = launch_finalize<MODE>(a.scratch, d.C, grid, T_all, d.nfft, d.F, d.avg_scale,
+                            d.onesided_mask ? 1 : 0, d.out, d.o_cs, d.out_kind,
+                            stream);
   if (launches)
     *launches += 2;
-  return cudaGetLastError();
+  return e;
 }
 
 // Every segment start 16-byte aligned (the cp.async staging condition).

@@ -387,65 +387,74 @@ __host__ __device__ inline int64_t flat_owner(int64_t j, int64_t T, int64_t n) {
 // Partials hold the one-sided bins k <= L/2 (PSD partials hold A[k] + A[L-k],
 // the pair average is the factor 1/2).  For real inputs the two-sided
 // spectrum is the conjugate mirror: P[L-k] = conj(P[k]).
-template <int MODE>
-__global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
-                                         int64_t C, int64_t nq, int64_t flat_T,
-                                         int64_t L, int64_t F, double avg_scale,
-                                         int onesided_mask, void *out,
-                                         int64_t o_cs, int out_kind) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= C * F)
-    return;
-  const int64_t FH = L / 2 + 1;
-  const int64_t c = i / F, k = i - c * F;
-  const bool mirror = k >= FH;
-  const int64_t kk = mirror ? L - k : k;
-  int64_t lo, hi;
+__device__ __forceinline__ void finalize_slots(int64_t c, int64_t C, int64_t nq,
+                                               int64_t flat_T, int64_t *lo,
+                                               int64_t *hi) {
   if (flat_T > 0) {
     const int64_t Tc = flat_T / C;
-    lo = flat_owner(c * Tc, flat_T, nq) + c;
-    hi = flat_owner((c + 1) * Tc - 1, flat_T, nq) + c + 1;
+    *lo = flat_owner(c * Tc, flat_T, nq) + c;
+    *hi = flat_owner((c + 1) * Tc - 1, flat_T, nq) + c + 1;
   } else {
-    lo = c * nq;
-    hi = lo + nq;
+    *lo = c * nq;
+    *hi = *lo + nq;
   }
-  double re = 0.0, im = 0.0;
+}
+
+// Slot values summed for one bin: s[0], s[1] (s[2] for coherence) of the
+// slots [q0, hi) with stride dq.
+template <int MODE>
+__device__ __forceinline__ void finalize_sum(const double *__restrict__ scratch,
+                                             int64_t FH, int64_t kk, int64_t q0,
+                                             int64_t hi, int64_t dq, double *s) {
+  if (MODE == ACC_COH) {
+    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
+    for (int64_t q = q0; q < hi; q += dq) {
+      const double2 a = s2[2 * (q * FH + kk)];
+      s[0] += a.x;
+      s[1] += a.y;
+      s[2] += s2[2 * (q * FH + kk) + 1].x;
+    }
+  } else if (MODE == ACC_PSD) {
+    for (int64_t q = q0; q < hi; q += dq)
+      s[0] += scratch[q * FH + kk];
+  } else {
+    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
+    for (int64_t q = q0; q < hi; q += dq) {
+      const double2 v = s2[q * FH + kk];
+      s[0] += v.x;
+      s[1] += v.y;
+    }
+  }
+}
+
+// Scale, mask and store output bin k of channel c from its summed slots.
+template <int MODE>
+__device__ __forceinline__ void finalize_store(const double *s, int64_t c,
+                                               int64_t k, int64_t F, bool mirror,
+                                               double avg_scale, int onesided_mask,
+                                               void *out, int64_t o_cs,
+                                               int out_kind) {
   if (MODE == ACC_COH) {
     // Reference coherence (spectral_analysis.cpp:199-221): Pxx, Pyy from
     // welch, Pxy = Re(csd) (the reference's csd returns the real part), all
     // with the same scale and mask; Cxy = Pxy^2 / max(Pxx Pyy, 1e-30), and 0
     // where Pxx Pyy <= 1e-30.
-    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
-    double sxx = 0.0, syy = 0.0, sxy = 0.0;
-    for (int64_t q = lo; q < hi; ++q) {
-      const double2 a = s2[2 * (q * FH + kk)];
-      sxx += a.x;
-      syy += a.y;
-      sxy += s2[2 * (q * FH + kk) + 1].x;
-    }
     double f = 0.25 * avg_scale; // partials are 4x the sums
     if (onesided_mask && k >= 1 && k <= F - 2)
       f *= 2.0;
-    const double pxx = sxx * f, pyy = syy * f, pxy = sxy * f;
+    const double pxx = s[0] * f, pyy = s[1] * f, pxy = s[2] * f;
     const double den = pxx * pyy;
     const double eps = 1e-30;
     reinterpret_cast<double *>(out)[c * o_cs + k] =
         den <= eps ? 0.0 : (pxy * pxy) / (den > eps ? den : eps);
     return;
   }
+  double re, im = 0.0;
   if (MODE == ACC_PSD) {
-    for (int64_t q = lo; q < hi; ++q)
-      re += scratch[q * FH + kk];
-    re *= 0.5;
+    re = s[0] * 0.5;
   } else {
-    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
-    for (int64_t q = lo; q < hi; ++q) {
-      const double2 v = s2[q * FH + kk];
-      re += v.x;
-      im += v.y;
-    }
-    re *= 0.25; // partials are 4 conj(X) Y
-    im *= 0.25;
+    re = s[0] * 0.25; // partials are 4 conj(X) Y
+    im = s[1] * 0.25;
     if (mirror)
       im = -im;
   }
@@ -473,6 +482,96 @@ __global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
     reinterpret_cast<double *>(out)[c * o_cs + k] = re;
     break;
   }
+}
+
+// One thread per output bin: for few slots per channel (many channels).
+template <int MODE>
+__global__ void spectral_finalize_kernel(const double *__restrict__ scratch,
+                                         int64_t C, int64_t nq, int64_t flat_T,
+                                         int64_t L, int64_t F, double avg_scale,
+                                         int onesided_mask, void *out,
+                                         int64_t o_cs, int out_kind) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= C * F)
+    return;
+  const int64_t FH = L / 2 + 1;
+  const int64_t c = i / F, k = i - c * F;
+  const bool mirror = k >= FH;
+  const int64_t kk = mirror ? L - k : k;
+  int64_t lo, hi;
+  finalize_slots(c, C, nq, flat_T, &lo, &hi);
+  double s[3] = {0.0, 0.0, 0.0};
+  finalize_sum<MODE>(scratch, FH, kk, lo, hi, 1, s);
+  finalize_store<MODE>(s, c, k, F, mirror, avg_scale, onesided_mask, out, o_cs,
+                       out_kind);
+}
+
+// Many slots per channel (few channels): a CTA of 32 x FW threads handles 32
+// consecutive output bins; warp w sums the slots lo + w, lo + w + FW, ...
+// (32 consecutive bins of one slot are one coalesced read), and warp 0 adds
+// the FW partial sums in warp order, so the result is deterministic.
+constexpr int kFinalizeWideWarps = 8;
+constexpr int kFinalizeWideFrom = 32; // slots per channel that select this kernel
+
+template <int MODE>
+__global__ void __launch_bounds__(32 * kFinalizeWideWarps)
+    spectral_finalize_wide_kernel(const double *__restrict__ scratch, int64_t C,
+                                  int64_t nq, int64_t flat_T, int64_t L,
+                                  int64_t F, double avg_scale, int onesided_mask,
+                                  void *out, int64_t o_cs, int out_kind) {
+  constexpr int FW = kFinalizeWideWarps;
+  __shared__ double part[FW][3][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t i = blockIdx.x * (int64_t)32 + lane;
+  const bool valid = i < C * F;
+  const int64_t FH = L / 2 + 1;
+  const int64_t c = valid ? i / F : 0, k = valid ? i - c * F : 0;
+  const bool mirror = k >= FH;
+  const int64_t kk = mirror ? L - k : k;
+  double s[3] = {0.0, 0.0, 0.0};
+  if (valid) {
+    int64_t lo, hi;
+    finalize_slots(c, C, nq, flat_T, &lo, &hi);
+    finalize_sum<MODE>(scratch, FH, kk, lo + w, hi, FW, s);
+  }
+  part[w][0][lane] = s[0];
+  part[w][1][lane] = s[1];
+  part[w][2][lane] = s[2];
+  __syncthreads();
+  if (w != 0 || !valid)
+    return;
+  double t[3] = {0.0, 0.0, 0.0};
+  for (int ww = 0; ww < FW; ++ww) {
+    t[0] += part[ww][0][lane];
+    t[1] += part[ww][1][lane];
+    t[2] += part[ww][2][lane];
+  }
+  finalize_store<MODE>(t, c, k, F, mirror, avg_scale, onesided_mask, out, o_cs,
+                       out_kind);
+}
+
+// Launch the finalize kernel that suits the slot count per channel.
+template <int MODE>
+cudaError_t launch_finalize(const double *scratch, int64_t C, int64_t nq,
+                            int64_t flat_T, int64_t L, int64_t F, double avg_scale,
+                            int onesided_mask, void *out, int64_t o_cs,
+                            int out_kind, cudaStream_t stream) {
+  const int64_t n = C * F;
+  // slots per channel: nq units, or about nq / C CTAs of the flat split
+  const int64_t per = flat_T > 0 ? (nq + C - 1) / C + 1 : nq;
+  if (per >= kFinalizeWideFrom) {
+    spectral_finalize_wide_kernel<MODE>
+        <<<(unsigned)((n + 31) / 32), 32 * kFinalizeWideWarps, 0, stream>>>(
+            scratch, C, nq, flat_T, L, F, avg_scale, onesided_mask, out, o_cs,
+            out_kind);
+  } else {
+    const int threads = 256;
+    spectral_finalize_kernel<MODE><<<(unsigned)((n + threads - 1) / threads),
+                                     threads, 0, stream>>>(
+        scratch, C, nq, flat_T, L, F, avg_scale, onesided_mask, out, o_cs,
+        out_kind);
+  }
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

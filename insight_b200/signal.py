@@ -44,6 +44,35 @@ def _is_torch(x) -> bool:
     return hasattr(x, "untyped_storage")
 
 
+def _stream_arg(stream, x):
+    """The cudaStream_t of a call: the caller's stream, else, for a CUDA
+    tensor input, torch's current stream on its device, so the call is
+    ordered after the work that produced the input (the backend's own stream
+    would not wait for it); None for host inputs."""
+    if stream is None:
+        if not (_is_torch(x) and x.is_cuda):
+            return None
+        import torch
+        stream = torch.cuda.current_stream(x.device)
+    h = stream if isinstance(stream, int) else stream.cuda_stream
+    # NULL selects the backend's own stream in the C ABI; torch's default
+    # stream is the legacy NULL stream, named explicitly as cudaStreamLegacy
+    return ctypes.c_void_p(h if h else _CUDA_STREAM_LEGACY)
+
+
+_CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy (driver_types.h)
+
+
+def _inputs_ready(*xs):
+    """The reference-signature functions are synchronous and run on the
+    backend's stream: let torch's pending work on CUDA inputs finish first."""
+    for x in xs:
+        if x is not None and _is_torch(x) and x.is_cuda:
+            import torch
+            torch.cuda.current_stream(x.device).synchronize()
+            return
+
+
 def _empty_like_place(x, shape, dtype: str):
     """Output buffer on x's place: numpy for host inputs, torch on x's device."""
     if _is_torch(x):
@@ -54,8 +83,25 @@ def _empty_like_place(x, shape, dtype: str):
     return np.empty(shape, dtype=dtype)
 
 
+_DESC_CACHE: dict = {}
+
+
 def _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
           scaling="density", mode="psd", axis=-1, seg_range=None, raw_sums=False):
+    """The call descriptor; repeated calls with the same arguments reuse one
+    (the backend only reads it)."""
+    key = (op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
+           scaling, mode, axis, seg_range, raw_sums)
+    d = _DESC_CACHE.get(key)
+    if d is None:
+        if len(_DESC_CACHE) >= 256:
+            _DESC_CACHE.clear()
+        d = _DESC_CACHE[key] = _make_desc(*key)
+    return d
+
+
+def _make_desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
+               scaling, mode, axis, seg_range, raw_sums):
     d = _abi.SpectralDesc()
     d.op = op
     d.axis = axis
@@ -139,9 +185,7 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
     if axes and op in (_abi.OP_SPECTROGRAM, _abi.OP_STFT):
         to = _empty_like_place(x, (S,), "float64")
         ta = _abi.as_array(to)
-    st = None
-    if stream is not None:
-        st = ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    st = _stream_arg(stream, x)
     _abi.check(_abi.lib().insight_b200_spectral(
         ctypes.byref(d), ctypes.byref(xa), _abi.ptr(ya), ctypes.byref(oa),
         _abi.ptr(fa), _abi.ptr(ta), st, 1 if sync else 0),
@@ -157,9 +201,7 @@ def finalize_sums(op, sums, n_seg, x_dtype, *, fs=1.0, window="hann", nperseg=25
     d = _desc(op, fs, window, nperseg, 0, nfft, "constant", return_onesided, scaling)
     sa = _abi.as_array(sums)
     dt = _abi.DT_F32 if str(x_dtype).endswith("float32") else _abi.DT_F64
-    st = None
-    if stream is not None:
-        st = ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    st = _stream_arg(stream, sums)
     _abi.check(_abi.lib().insight_b200_finalize_sums(
         ctypes.byref(d), int(n_seg), dt, ctypes.byref(sa), st), "finalize_sums")
     return sums
@@ -181,6 +223,7 @@ def csd(x, y, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
     shape = (x.shape[0], F) if x.ndim == 2 else (F,)
     pxy = _empty_like_place(x, shape, "float64")
     f = _empty_like_place(x, (F,), "float64")
+    _inputs_ready(x, y)
     _abi.check(_abi.lib().insight_b200_csd(
         ctypes.byref(xa), ctypes.byref(ya), float(fs), window.encode(), int(nperseg),
         int(noverlap or 0), int(nfft or 0), detrend.encode(),
@@ -197,6 +240,7 @@ def welch(x, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
     shape = (x.shape[0], F) if x.ndim == 2 else (F,)
     pxx = _empty_like_place(x, shape, "float64")
     f = _empty_like_place(x, (F,), "float64")
+    _inputs_ready(x)
     _abi.check(_abi.lib().insight_b200_welch(
         ctypes.byref(xa), float(fs), window.encode(), int(nperseg),
         int(noverlap or 0), int(nfft or 0), detrend.encode(),
@@ -214,6 +258,7 @@ def coherence(x, y, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None
     shape = (x.shape[0], F) if x.ndim == 2 else (F,)
     cxy = _empty_like_place(x, shape, "float64")
     f = _empty_like_place(x, (F,), "float64")
+    _inputs_ready(x, y)
     _abi.check(_abi.lib().insight_b200_coherence(
         ctypes.byref(xa), ctypes.byref(ya), float(fs), window.encode(), int(nperseg),
         int(noverlap or 0), int(nfft or 0), detrend.encode(),
@@ -230,6 +275,7 @@ def periodogram(x, fs=1.0, window="boxcar", nfft=None, detrend="constant",
     shape = (x.shape[0], F) if x.ndim == 2 else (F,)
     pxx = _empty_like_place(x, shape, "float64")
     f = _empty_like_place(x, (F,), "float64")
+    _inputs_ready(x)
     _abi.check(_abi.lib().insight_b200_periodogram(
         ctypes.byref(xa), float(fs), window.encode(), int(nfft or 0),
         detrend.encode(), 1 if return_onesided else 0, scaling.encode(),
@@ -252,9 +298,7 @@ def istft(Zxx, fs=1.0, window="hann", nperseg=0, noverlap=0, nfft=0, *,
             int(nfft or 0), ctypes.byref(c), ctypes.byref(n)), "istft")
         shape = (c.value, n.value) if Zxx.ndim == 3 else (n.value,)
         out = _empty_like_place(Zxx, shape, "float64")
-    st = None
-    if stream is not None:
-        st = ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    st = _stream_arg(stream, Zxx)
     _abi.check(_abi.lib().insight_b200_istft_async(
         ctypes.byref(za), window.encode(), int(nperseg or 0), int(noverlap or 0),
         int(nfft or 0), ctypes.byref(_abi.as_array(out)), st, 1 if sync else 0),
@@ -271,6 +315,7 @@ def spectrogram(x, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
     sxx = _empty_like_place(x, shape, "float64")
     f = _empty_like_place(x, (F,), "float64")
     t = _empty_like_place(x, (S,), "float64")
+    _inputs_ready(x)
     _abi.check(_abi.lib().insight_b200_spectrogram(
         ctypes.byref(_abi.as_array(x)), float(fs), window.encode(), int(nperseg),
         int(noverlap or 0), int(nfft or 0), detrend.encode(),
@@ -298,6 +343,7 @@ def stft(x, fs=1.0, window="hann", nperseg=256, noverlap=None, nfft=None,
     z = _empty_like_place(x, shape, dt)
     f = _empty_like_place(x, (F,), "float64")
     t = _empty_like_place(x, (S,), "float64")
+    _inputs_ready(x)
     _abi.check(_abi.lib().insight_b200_stft(
         ctypes.byref(_abi.as_array(x)), float(fs), window.encode(), int(nperseg),
         int(noverlap or 0), int(nfft or 0), ctypes.byref(_abi.as_array(f)),

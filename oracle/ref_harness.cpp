@@ -363,15 +363,18 @@ int ref_gpu_stft(const void *x, int64_t n, int dtype, double fs,
     const int64_t S = n >= nperseg ? (n - nperseg) / step + 1 : 0;
     const int64_t F = nfft / 2 + 1;
     ins::Array wg = ins::signal::get_window(window, nperseg, false).to(gpu);
+    // the (n_freq, n_seg) buffer, passed as the (n_seg, n_freq) transposed
+    // view the reference returns (spectral_analysis.cpp:256,321)
     ins::Array out(ins::Shape({F, S}), ins::DType::F64, gpu); // fully written
+    ins::Array view = out.transpose({1, 0});
     int32_t dcode = 0, os = 1, mode = 1;
     double sc = 1.0;
     int64_t axis = -1;
     ins::ops().launch("stft", gpu, xg.dtype(),
-                      {out.layout_ptr(), xg.layout_ptr(), wg.layout_ptr(),
+                      {view.layout_ptr(), xg.layout_ptr(), wg.layout_ptr(),
                        &nperseg, &noverlap, &nfft, &dcode, &os, &mode, &sc,
                        &axis},
-                      {out.layout_ptr()});
+                      {view.layout_ptr()});
     *n_seg = S;
     *n_freq = F;
     copy_out(out, s_out, cap);

@@ -33,6 +33,15 @@ def test_async_call_returns_while_another_stream_runs(cuda):
     xb = torch.randn((8, 1 << 18), generator=g, device=cuda)
     pb = torch.empty((8, 1025), dtype=torch.float64, device=cuda)
     kwb = dict(fs=7.0, window="nuttall", nperseg=1999, noverlap=1000, nfft=2048)
+    # CUDA loads each kernel on its first launch in a process (lazy module
+    # loading), which may synchronise the context: run both kernel shapes
+    # once first (B's with another window, on another stream, so its tables
+    # and its stream's scratch are still new in the timed call)
+    warm = torch.cuda.Stream(cuda)
+    ib.spectral(ib.OP_STFT, x[:2], complex_output=True, nperseg=L, noverlap=L - H,
+                stream=warm)
+    ib.spectral(ib.OP_WELCH, xb, stream=warm, axes=True,
+                **dict(kwb, window="hann"))
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     torch.cuda.synchronize()
     ev[0].record(sa)
