@@ -60,7 +60,7 @@ WORKLOADS = {
                      "signal::stft {C} ch x 2^22 f32, nperseg 2048, hop 512, "
                      "hann, complex64 out ({C}, 1025, 8189)")),
     "welch": dict(op="welch", C=1, N=1 << 20, L=1024, H=512, window="hann",
-                  dtype="f32", fs=1.0e4, detrend="constant", desc=(
+                  dtype="f32", fs=1.0e4, detrend="constant", plan=True, desc=(
                       "signal::welch {C} ch x 2^20 f32, nperseg 1024, "
                       "noverlap 512, hann, constant detrend, density")),
     "welch_f64": dict(op="welch", C=1024, N=1 << 20, L=4096, H=2048,
@@ -500,7 +500,18 @@ def setup(torch, w, dev, rank, world, stream):
 
         def call(xin, yin, o):
             ib.spectral(ib.OP_WELCH, xin, out=o, detrend=w["detrend"], **kw)
-    st.update(step=lambda on_phase=None: call(x, y, out), call=call, x=x, y=y,
+    step = lambda on_phase=None: call(x, y, out)
+    if w.get("plan"):
+        # a short signal: the call is bound by host work and launch latency,
+        # so the step replays it as a captured CUDA graph (SpectralPlan); the
+        # regular call is timed beside it
+        plan = ib.SpectralPlan(
+            ib.OP_WELCH, x, out=out, detrend=w["detrend"],
+            **{k: v for k, v in kw.items() if k not in ("sync", "axes")})
+        st["plan"] = plan
+        st["call_step"] = step
+        step = lambda on_phase=None: plan.run(stream=stream)
+    st.update(step=step, call=call, x=x, y=y,
               out=out, two=two, samples_total=samples_total, in_bytes=in_bytes,
               out_bytes=out_bytes, transforms=transforms, C_local=C,
               parallelism=par, scaling=scaling, detail={"channels_per_gpu": C})
@@ -606,8 +617,15 @@ def measure_extra(torch, R, name, dev, stream, steps, warmup):
            "gpu_launches": launches, "clocks": clocks,
            "roofline": roofline_of(w, st, ms_local)}
     res.update(st["detail"])
+    if "call_step" in st:
+        cms, _, _, _ = timed(torch, R, stream, st["call_step"], steps, warmup)
+        res["plan"] = ("value and ms_per_step replay the call as a captured CUDA "
+                       "graph (SpectralPlan); ms_per_step_call is the regular call")
+        res["ms_per_step_call"] = cms
     if name == "welch_long":
         res["breakdown"] = phase_breakdown(torch, R, stream, st["step"], steps)
+    if "plan" in st:
+        st["plan"].close()
     del st
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -643,6 +661,10 @@ def run_ours(args, w):
     breakdown = None
     if w["name"] == "welch_long":
         breakdown = phase_breakdown(torch, R, stream, st["step"], args.steps)
+    call_ms = None
+    if "call_step" in st:
+        call_ms, _, _, _ = timed(torch, R, stream, st["call_step"], args.steps,
+                                 args.warmup)
 
     # end to end through the public API with pinned host buffers
     e2e = None
@@ -662,7 +684,9 @@ def run_ours(args, w):
                         "result copied out every step, in channel chunks that "
                         "overlap the copies with the kernels")}
         del xh, yh, oh
-    for k in ("x", "y", "out", "step", "call"):
+    if "plan" in st:
+        st.pop("plan").close()
+    for k in ("x", "y", "out", "step", "call", "call_step"):
         st.pop(k, None)
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -710,6 +734,11 @@ def run_ours(args, w):
         }
         if breakdown is not None:
             line["breakdown"] = breakdown
+        if call_ms is not None:
+            line["plan"] = ("value and ms_per_step replay the call as a captured "
+                            "CUDA graph (SpectralPlan); ms_per_step_call is the "
+                            "regular call")
+            line["ms_per_step_call"] = call_ms
         if extras:
             line["workloads"] = extras
         print(json.dumps(line), flush=True)

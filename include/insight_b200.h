@@ -429,6 +429,30 @@ INSIGHT_B200_API C_Status insight_b200_spectral(
     const InsightArray *y, InsightArray *out, InsightArray *f, InsightArray *t,
     void *stream, int sync);
 
+/* A plan: one insight_b200_spectral call captured into a CUDA graph.  No
+ * counterpart in the reference (its spectral ops are per-call composites).
+ * For callers that repeat the same call on the same GPU arrays and are
+ * bound by launch and host overhead (short signals, tight loops): executing
+ * a plan is one graph launch instead of the call's host-side planning and
+ * kernel launches.
+ * plan_create takes the arguments of insight_b200_spectral (x, y, out must
+ * be GPU arrays; no f / t axes), runs the call once on the plan's own
+ * stream (ordered after `stream`, NULL: none), then captures it.  The plan
+ * keeps the arrays' device addresses: each execution recomputes out from
+ * the current contents of x (and y).  It owns its working buffers, so
+ * executions of one plan must not overlap on the GPU (different plans may).
+ * plan_execute launches the graph on `stream` (NULL: the plan's stream) and
+ * returns at once (sync == 0) or after the stream has finished (sync != 0).
+ * plan_destroy waits for the device, then releases the plan. */
+typedef struct InsightB200Plan InsightB200Plan;
+INSIGHT_B200_API C_Status insight_b200_plan_create(
+    const InsightB200SpectralDesc *desc, const InsightArray *x,
+    const InsightArray *y, InsightArray *out, void *stream,
+    InsightB200Plan **plan);
+INSIGHT_B200_API C_Status insight_b200_plan_execute(InsightB200Plan *plan,
+                                                    void *stream, int sync);
+INSIGHT_B200_API C_Status insight_b200_plan_destroy(InsightB200Plan *plan);
+
 /* Scale and mask F64 raw sums of welch/csd (raw_sums = 1) in place after
  * they were reduced across devices: out = sums * scale / n_seg * m[k].
  * sums is a GPU array [n_freq] or [C, n_freq] (F64, or C64 for complex

@@ -7,8 +7,8 @@ sm_100a kernel family behind
 Insight's device-plugin C ABI (include/insight_b200.h).
 """
 from . import _abi  # noqa: F401
-from .signal import (SpectralResult, SpectrogramResult, coherence, csd,  # noqa: F401
-                     finalize_sums, istft, periodogram, spectral,
+from .signal import (SpectralPlan, SpectralResult, SpectrogramResult,  # noqa: F401
+                     coherence, csd, finalize_sums, istft, periodogram, spectral,
                      spectral_shape, spectrogram, stft, welch)
 
 OP_WELCH = _abi.OP_WELCH

@@ -124,6 +124,9 @@ EXPORTS = (
     "insight_b200_finalize_sums",
     "insight_b200_launch_count",
     "insight_b200_welch_noalloc",
+    "insight_b200_plan_create",
+    "insight_b200_plan_execute",
+    "insight_b200_plan_destroy",
 )
 
 _lib = None
@@ -189,6 +192,14 @@ def lib() -> ctypes.CDLL:
             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_char_p,
             ctypes.c_int32, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p]
         L.insight_b200_welch_noalloc.restype = ctypes.c_int
+        L.insight_b200_plan_create.argtypes = [PD, PA, PA, PA, ctypes.c_void_p,
+                                               ctypes.POINTER(ctypes.c_void_p)]
+        L.insight_b200_plan_execute.argtypes = [ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_int]
+        L.insight_b200_plan_destroy.argtypes = [ctypes.c_void_p]
+        for n in ("insight_b200_plan_create", "insight_b200_plan_execute",
+                  "insight_b200_plan_destroy"):
+            getattr(L, n).restype = ctypes.c_int
         for n in ("insight_b200_welch", "insight_b200_csd", "insight_b200_spectrogram",
                   "insight_b200_stft", "insight_b200_coherence",
                   "insight_b200_periodogram", "insight_b200_istft_shape",

@@ -398,6 +398,35 @@ template <typename T, int L, int E> struct ThreadTw1 {
   __host__ __device__ static constexpr int stride() { return total() | 1; }
 };
 
+// Shape condition of the warp-shuffle last pass (fft_group_w1_lastshfl):
+// last radix 2, one radix-E butterfly per thread in the pass before it.
+template <int L, int E> struct LastShfl {
+  using PL = Plan<L, E>;
+  static constexpr int NP = PL::passes();
+  static constexpr int RP = PL::radix(NP - 2);  // radix of the pass before
+  static constexpr int NSP = PL::ns(NP - 2);
+  static constexpr bool ok = NP >= 2 && PL::radix(NP - 1) == 2 && RP == E &&
+                             NSP * RP == L / 2 && NSP % 16 == 0 &&
+                             (L / E) % 32 == 0;
+};
+
+// Lane l of warp w takes butterfly m + h*NSP with h = bit 4 of l and
+// m = 16 w + (l & 15): partners are 16 lanes apart (one exchange over lane
+// bit 4), and each half-warp reads 16 consecutive butterflies, so the 8-byte
+// shared-memory loads of a half-warp fall on 16 distinct bank pairs.
+__host__ __device__ constexpr int shfl_half(int t) { return (t >> 4) & 1; }
+__host__ __device__ constexpr int shfl_m(int t) { return (t >> 5) * 16 + (t & 15); }
+
+template <int L, int E>
+__host__ __device__ constexpr int shfl_j(int t) {
+  return shfl_half(t) * LastShfl<L, E>::NSP + shfl_m(t);
+}
+
+template <int L, int E>
+__host__ __device__ constexpr int shfl_bin(int t, int e) {
+  return shfl_half(t) * (L / 2) + shfl_m(t) + LastShfl<L, E>::NSP * bitrev<E>(e);
+}
+
 // Mirrored butterfly assignment of the last pass.  Butterfly j of the last
 // pass (radix R, NS = L/R) yields bins j + NS*r, whose mirrors L - bin are
 // the bins of butterfly NS - j (element R-1-r), or of j itself for j = 0
@@ -415,7 +444,8 @@ __host__ __device__ constexpr int pair_j(int t, int b) {
   return j == 0 ? NS / 2 : NS - j;
 }
 
-template <typename T, int L, int E, int P, typename V, bool PAIRS = false>
+template <typename T, int L, int E, int P, typename V, bool PAIRS = false,
+          bool SHFL = false>
 __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
                                                int nthreads) {
   using PL = Plan<L, E>;
@@ -431,8 +461,15 @@ __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
       constexpr int NS = PL::ns(p);
       if (slot >= TT::offset(p) && slot < TT::offset(p + 1)) {
         const int b = slot - TT::offset(p);
-        const int j =
-            (PAIRS && p == NPASS - 1) ? pair_j<L, E, P>(tt, b) : tt + b * P;
+        int j;
+        if constexpr (PAIRS && p == NPASS - 1)
+          j = pair_j<L, E, P>(tt, b);
+        else if constexpr (SHFL && p == NPASS - 2)
+          j = shfl_j<L, E>(tt);
+        else if constexpr (SHFL && p == NPASS - 1)
+          j = shfl_m(tt); // the shuffle pass uses W_L^m from slot 0
+        else
+          j = tt + b * P;
         const int k = j & (NS - 1);
         val = tw[k * (L / (NS * R))];
       }
@@ -511,6 +548,73 @@ __device__ __forceinline__ void fft_group_w1_pairs(V *v, V *buf, int t, int g,
       pass_store<L, E, P, p>(v, buf, t);
       group_sync<G, P>(g);
     }
+  });
+}
+
+// Last pass on warp shuffles.  When the last radix is 2 and the pass before
+// it gives every thread one butterfly (radix E, L/E = P butterflies, whose
+// outputs lie NS*E = L/2 apart for butterflies j and j + NS), thread t takes
+// butterfly shfl_j(t) = h*NS + m of that pass (h, m: shfl_half, shfl_m):
+// the two lanes with the same m then hold the outputs m + NS*r and
+// L/2 + m + NS*r, the two inputs of a radix-2 butterfly of the last pass, in
+// the same register r.  The last pass is one exchange between those lanes
+// (__shfl_xor_sync over lane bit 4) instead of a shared-memory round trip and
+// a group barrier:
+//   X[j] = a + w b,  X[j + L/2] = a - w b,   j = m + NS*r,  w = W_L^j,
+// where the h = 1 lane forms w b with w = W_L^m W_{2E}^r (W_L^{NS} = W_{2E})
+// and both lanes swap their values.  After it, register e of thread t holds
+// bin shfl_bin(t, e).  The twiddle rows come from fill_thread_w1 with SHFL =
+// true (the pass before the last holds W^k of butterfly shfl_j(t), the last
+// pass W_L^m in its first slot).  A group must be whole warps.
+template <typename T, int L, int E, int P, int G, typename V>
+__device__ __forceinline__ void fft_group_w1_lastshfl(V *v, V *buf, int t, int g,
+                                                      const V *row1) {
+  using PL = Plan<L, E>;
+  using LS = LastShfl<L, E>;
+  using TT = ThreadTw1<T, L, E>;
+  constexpr int NP = LS::NP;
+  constexpr int NSP = LS::NSP;
+  static_assert(LS::ok && P == L / E, "shuffle last pass");
+  static_for<0, NP - 1>([&](auto pIC) {
+    constexpr int p = decltype(pIC)::value;
+    if constexpr (p > 0 && p < NP - 2) {
+      pass_load<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    } else if constexpr (p > 0) { // p == NP - 2: butterfly shfl_j(t)
+      const int j = shfl_j<L, E>(t);
+      static_for<0, E>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        if constexpr ((L / E) % 16 == 0)
+          v[r] = buf[spad(j) + pad_off<r * (L / E)>()];
+        else
+          v[r] = buf[spad(j + r * (L / E))];
+      });
+      group_sync<G, P>(g);
+    }
+    pass_compute_w1<T, L, E, P, p>(v, row1);
+    if constexpr (p + 2 < NP) {
+      pass_store<L, E, P, p>(v, buf, t);
+      group_sync<G, P>(g);
+    }
+  });
+  // v[bitrev(r)] = output r of butterfly shfl_j(t) = element
+  // h * L/2 + m + NSP * r of the last pass's input
+  const bool odd = shfl_half(t) != 0;
+  const V wm = row1[TT::offset(NP - 1)]; // W_L^m
+  const T sgn = odd ? T(-1) : T(1);
+  static_for<0, E>([&](auto rIC) {
+    constexpr int r = decltype(rIC)::value;
+    constexpr int e = bitrev<E>(r);
+    // W_L^{NSP r} = W_{2E}^r = W_32^{r * 32 / (2E)}
+    static_assert(L / NSP == 2 * E && 2 * E <= 32, "twiddle step");
+    const V wr = mul_w32<T, (r * 32 / (2 * E)) % 32>(wm);
+    const V f = odd ? wr : V{T(1), T(0)};
+    const V own = vmul(v[e], f);
+    V recv;
+    recv.x = __shfl_xor_sync(0xffffffffu, own.x, 16);
+    recv.y = __shfl_xor_sync(0xffffffffu, own.y, 16);
+    // h = 0 lane: a + w b = own + recv; h = 1 lane: a - w b = recv - own
+    v[e] = {fma(sgn, own.x, recv.x), fma(sgn, own.y, recv.y)};
   });
 }
 

@@ -36,6 +36,10 @@ namespace ib200 {
 namespace {
 thread_local std::string g_last_error;
 std::atomic<int64_t> g_launches{0};
+// True while this thread captures a call into a plan's CUDA graph: the call
+// then only enqueues kernels (its tables and buffers were made by the plan's
+// warm-up run), without event waits, event records or allocations.
+thread_local bool g_capturing = false;
 } // namespace
 
 void set_last_error(const std::string &msg) { g_last_error = msg; }
@@ -140,6 +144,7 @@ DeviceState &device_state(int dev) {
 void ensure(DevBuf &b, size_t bytes, cudaStream_t stream) {
   if (b.n >= bytes && b.p)
     return;
+  check(!g_capturing, "plan: a buffer would grow while the call is captured");
   if (b.p) {
     cuda_check(cudaFreeAsync(b.p, stream), "cudaFreeAsync");
     b.p = nullptr;
@@ -153,6 +158,8 @@ void ensure(DevBuf &b, size_t bytes, cudaStream_t stream) {
 // The per-stream working buffers of `stream`, ordered after their last use.
 StreamBufs &stream_bufs(DeviceState &st, cudaStream_t stream) {
   StreamBufs &sb = st.per_stream[stream];
+  if (g_capturing)
+    return sb;
   if (!sb.last)
     cuda_check(cudaEventCreateWithFlags(&sb.last, cudaEventDisableTiming),
                "cudaEventCreate");
@@ -162,7 +169,8 @@ StreamBufs &stream_bufs(DeviceState &st, cudaStream_t stream) {
 }
 
 void mark_used(StreamBufs &sb, cudaStream_t stream) {
-  cuda_check(cudaEventRecord(sb.last, stream), "cudaEventRecord");
+  if (!g_capturing)
+    cuda_check(cudaEventRecord(sb.last, stream), "cudaEventRecord");
 }
 
 size_t dtype_size(int32_t dt) {
@@ -193,10 +201,12 @@ const void *table(DeviceState &st, const std::string &key,
                   std::vector<unsigned char> bytes, cudaStream_t stream) {
   auto it = st.tables.find(key);
   if (it != st.tables.end()) {
-    cuda_check(cudaStreamWaitEvent(stream, it->second.ready, 0),
-               "cudaStreamWaitEvent");
+    if (!g_capturing)
+      cuda_check(cudaStreamWaitEvent(stream, it->second.ready, 0),
+                 "cudaStreamWaitEvent");
     return it->second.buf.p;
   }
+  check(!g_capturing, "plan: a table would be uploaded while the call is captured");
   Table &t = st.tables[key];
   t.host = std::move(bytes);
   ensure(t.buf, t.host.size(), stream);
@@ -958,6 +968,134 @@ C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums) {
     set_last_error(e.what());
     return C_FAILED;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Plans: one call captured into a CUDA graph.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int dev = 0;
+  cudaStream_t cs = nullptr; // capture stream (owns the plan's scratch)
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  DevBuf scratch, frames;    // taken over from the capture stream's buffers
+};
+
+C_Status plan_create(const Call &c0, void **plan_out) {
+  Plan *pl = nullptr;
+  try {
+    check(plan_out != nullptr, "plan: output handle is NULL");
+    check(c0.x && c0.x->device_type == INSIGHT_DEVICE_GPU && c0.out &&
+              c0.out->device_type == INSIGHT_DEVICE_GPU &&
+              (!c0.y || c0.y->device_type == INSIGHT_DEVICE_GPU),
+          "plan: inputs and output must be GPU arrays");
+    check(!c0.f && !c0.t, "plan: the f and t axes are not part of a plan");
+    pl = new Plan();
+    pl->dev = c0.x->device_id;
+    cuda_check(cudaSetDevice(pl->dev), "cudaSetDevice");
+    cuda_check(cudaStreamCreateWithFlags(&pl->cs, cudaStreamNonBlocking),
+               "cudaStreamCreate");
+    // order the plan after the caller's stream, then run the call once on
+    // the capture stream: tables uploaded, the stream's scratch allocated
+    if (c0.stream) {
+      cudaEvent_t ev;
+      cuda_check(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming),
+                 "cudaEventCreate");
+      cuda_check(cudaEventRecord(ev, c0.stream), "cudaEventRecord");
+      cuda_check(cudaStreamWaitEvent(pl->cs, ev, 0), "cudaStreamWaitEvent");
+      cuda_check(cudaEventDestroy(ev), "cudaEventDestroy");
+    }
+    Call c = c0;
+    c.stream = pl->cs;
+    c.sync = true;
+    if (run(c) != C_SUCCESS)
+      throw Fail(last_error());
+    // capture the same call
+    c.sync = false;
+    cuda_check(cudaStreamBeginCapture(pl->cs, cudaStreamCaptureModeThreadLocal),
+               "cudaStreamBeginCapture");
+    g_capturing = true;
+    const C_Status rs = run(c);
+    g_capturing = false;
+    const cudaError_t ec = cudaStreamEndCapture(pl->cs, &pl->graph);
+    if (rs != C_SUCCESS)
+      throw Fail(last_error());
+    cuda_check(ec, "cudaStreamEndCapture");
+    cuda_check(cudaGraphInstantiate(&pl->exec, pl->graph, 0),
+               "cudaGraphInstantiate");
+    // the plan owns the buffers its graph writes
+    DeviceState &st = device_state(pl->dev);
+    {
+      std::lock_guard<std::mutex> lk(st.mu);
+      auto it = st.per_stream.find(pl->cs);
+      if (it != st.per_stream.end()) {
+        pl->scratch = it->second.scratch;
+        pl->frames = it->second.frames;
+        if (it->second.last)
+          cudaEventDestroy(it->second.last);
+        st.per_stream.erase(it);
+      }
+    }
+    *plan_out = pl;
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    g_capturing = false;
+    set_last_error(e.what());
+    if (pl)
+      plan_destroy(pl);
+    return C_FAILED;
+  }
+}
+
+C_Status plan_execute(void *plan, cudaStream_t stream, bool sync) {
+  try {
+    check(plan != nullptr, "plan: handle is NULL");
+    Plan *pl = static_cast<Plan *>(plan);
+    cuda_check(cudaSetDevice(pl->dev), "cudaSetDevice");
+    cudaStream_t s = stream ? stream : pl->cs;
+    cuda_check(cudaGraphLaunch(pl->exec, s), "cudaGraphLaunch");
+    g_launches += 1;
+    if (sync)
+      cuda_check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return C_SUCCESS;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return C_FAILED;
+  }
+}
+
+C_Status plan_destroy(void *plan) {
+  if (!plan)
+    return C_SUCCESS;
+  Plan *pl = static_cast<Plan *>(plan);
+  cudaSetDevice(pl->dev);
+  // executions may have been queued on any stream: let the device finish
+  // them before the buffers their kernels write are released
+  cudaDeviceSynchronize();
+  if (pl->exec)
+    cudaGraphExecDestroy(pl->exec);
+  if (pl->graph)
+    cudaGraphDestroy(pl->graph);
+  if (pl->cs) {
+    if (pl->scratch.p)
+      cudaFreeAsync(pl->scratch.p, pl->cs);
+    if (pl->frames.p)
+      cudaFreeAsync(pl->frames.p, pl->cs);
+    cudaStreamSynchronize(pl->cs);
+  }
+  if (pl->cs) {
+    DeviceState &st = device_state(pl->dev);
+    std::lock_guard<std::mutex> lk(st.mu);
+    auto it = st.per_stream.find(pl->cs);
+    if (it != st.per_stream.end()) {
+      if (it->second.last)
+        cudaEventDestroy(it->second.last);
+      st.per_stream.erase(it);
+    }
+    cudaStreamDestroy(pl->cs);
+  }
+  delete pl;
+  return C_SUCCESS;
 }
 
 } // namespace ib200

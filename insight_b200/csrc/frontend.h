@@ -57,6 +57,12 @@ C_Status shape(const Call &c, int64_t *n_channels, int64_t *n_seg,
                int64_t *n_freq);
 C_Status finalize_sums(const Call &c, int64_t S_total, InsightArray *sums);
 
+// One call (GPU arrays only) captured into a CUDA graph; executing the plan
+// replays the call's kernels on the arrays it was made with.
+C_Status plan_create(const Call &c, void **plan);
+C_Status plan_execute(void *plan, cudaStream_t stream, bool sync);
+C_Status plan_destroy(void *plan);
+
 void set_last_error(const std::string &msg);
 const char *last_error();
 int64_t launch_count();

@@ -932,6 +932,33 @@ C_Status insight_b200_spectral(const InsightB200SpectralDesc *desc,
   return ib200::run(c);
 }
 
+C_Status insight_b200_plan_create(const InsightB200SpectralDesc *desc,
+                                  const InsightArray *x, const InsightArray *y,
+                                  InsightArray *out, void *stream,
+                                  InsightB200Plan **plan) {
+  if (!desc || !plan) {
+    set_last_error("plan: desc or plan handle is NULL");
+    return C_FAILED;
+  }
+  ib200::Call c = from_desc(desc);
+  c.x = x;
+  c.y = y;
+  c.out = out;
+  c.stream = (cudaStream_t)stream;
+  void *p = nullptr;
+  const C_Status s = ib200::plan_create(c, &p);
+  *plan = static_cast<InsightB200Plan *>(p);
+  return s;
+}
+
+C_Status insight_b200_plan_execute(InsightB200Plan *plan, void *stream, int sync) {
+  return ib200::plan_execute(plan, (cudaStream_t)stream, sync != 0);
+}
+
+C_Status insight_b200_plan_destroy(InsightB200Plan *plan) {
+  return ib200::plan_destroy(plan);
+}
+
 C_Status insight_b200_finalize_sums(const InsightB200SpectralDesc *desc,
                                     int64_t n_seg, int32_t x_dtype,
                                     InsightArray *sums, void *stream) {

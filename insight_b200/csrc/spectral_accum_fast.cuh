@@ -76,6 +76,18 @@ __device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
 #ifndef IB200_ACC_MIR
 #define IB200_ACC_MIR 1
 #endif
+// SHF (welch with first-twiddle rows, last radix 2 after a radix-E pass,
+// groups of whole warps: nperseg 8192 in f32 and f64, 512 in f32, 1024 in
+// f64): the last pass runs on warp shuffles (fft_group_w1_lastshfl), one
+// shared-memory exchange and one group barrier fewer per transform.
+#ifndef IB200_ACC_SHFL
+#define IB200_ACC_SHFL 1
+#endif
+template <typename T, int L, int E>
+__host__ __device__ constexpr bool acc_shfl(int mode, int twm) {
+  return IB200_ACC_SHFL && mode == ACC_PSD && twm == 1 &&
+         LastShfl<L, E>::ok && (L / E) % 32 == 0;
+}
 template <typename T, int L, int E>
 __host__ __device__ constexpr bool acc_mirrored(int mode, int twm) {
   return IB200_ACC_MIR && mode != ACC_PSD && twm == 1 &&
@@ -101,6 +113,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   constexpr int NF = MODE == ACC_PSD ? NACC : 1; // f32 partial accumulators
   static_assert(SH >= 0 && SH < R0, "overlap shift");
   constexpr bool MIR = acc_mirrored<T, L, E>(MODE, TWM);
+  constexpr bool SHF = acc_shfl<T, L, E>(MODE, TWM);
   constexpr int RL = PL::radix(PL::passes() - 1); // last-pass radix
   constexpr int NSL = L / RL;
   constexpr int HB = E / RL / 2; // mirrored butterfly pairs per thread
@@ -129,7 +142,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   else if constexpr (TWM == 1)
-    fill_thread_w1<T, L, E, P, V, MIR>(tws, p.tw, threadIdx.x, NT);
+    fill_thread_w1<T, L, E, P, V, MIR, SHF>(tws, p.tw, threadIdx.x, NT);
   __syncthreads();
   const V *row = tws + t * TWROW;
   // MIR: bin of accumulator slot s (s < E/2: butterfly pair h = s / RL,
@@ -198,6 +211,8 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   auto fft = [&](V(&v)[E], V *b) {
     if constexpr (MIR)
       fft_group_w1_pairs<T, L, E, P, G>(v, b, t, g, row);
+    else if constexpr (SHF)
+      fft_group_w1_lastshfl<T, L, E, P, G>(v, b, t, g, row);
     else if constexpr (TWM == 2)
       fft_group_tw_m<T, L, E, P, G, 1>(&v, b, GS, t, g, row);
     else if constexpr (TWM == 1)
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
       double *sm = reinterpret_cast<double *>(buf);
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        sm[out_bin<L, E, P>(t, e)] = acc[e];
+        sm[SHF ? shfl_bin<L, E>(t, e) : out_bin<L, E, P>(t, e)] = acc[e];
       __syncthreads();
       for (int k = threadIdx.x; k < FH; k += NT) {
         double s = 0.0;

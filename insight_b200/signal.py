@@ -24,7 +24,7 @@ from . import _abi
 
 __all__ = ["SpectralResult", "SpectrogramResult", "welch", "csd", "coherence",
            "periodogram", "spectrogram", "stft", "istft", "spectral",
-           "spectral_shape", "finalize_sums"]
+           "spectral_shape", "finalize_sums", "SpectralPlan"]
 
 
 @dataclass
@@ -193,6 +193,52 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
     if op in (_abi.OP_WELCH, _abi.OP_CSD, _abi.OP_COHERENCE):
         return fo, out
     return fo, to, out
+
+
+class SpectralPlan:
+    """One ``spectral`` call on fixed CUDA tensors, captured into a CUDA
+    graph (insight_b200_plan_create).  ``run()`` replays the call's kernels
+    with one graph launch: for loops that repeat the same call on the same
+    tensors and would otherwise be bound by per-call host work and launch
+    latency (short signals).  Each run recomputes ``out`` from the current
+    contents of ``x`` (and ``y``); runs of one plan must not overlap on the
+    GPU.  The arguments are those of ``spectral`` (``out`` required, no f /
+    t axes)."""
+
+    def __init__(self, op, x, y=None, *, out, fs=1.0, window="hann", nperseg=256,
+                 noverlap=None, nfft=None, detrend="constant", return_onesided=True,
+                 scaling="density", mode="psd", axis=-1, seg_range=None,
+                 raw_sums=False, stream=None):
+        self._h = None
+        d = _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
+                  scaling, mode, axis, seg_range, raw_sums)
+        xa, ya, oa = _abi.as_array(x), _abi.as_array(y), _abi.as_array(out)
+        h = ctypes.c_void_p()
+        _abi.check(_abi.lib().insight_b200_plan_create(
+            ctypes.byref(d), ctypes.byref(xa), _abi.ptr(ya), ctypes.byref(oa),
+            _stream_arg(stream, x), ctypes.byref(h)), "SpectralPlan")
+        self._h = h
+        self._keep = (x, y, out, d)
+        self.out = out
+
+    def run(self, stream=None, sync=False):
+        """Launch the captured call on ``stream`` (default: torch's current
+        stream of x's device); returns ``out``."""
+        _abi.check(_abi.lib().insight_b200_plan_execute(
+            self._h, _stream_arg(stream, self._keep[0]), 1 if sync else 0),
+            "SpectralPlan.run")
+        return self.out
+
+    def close(self):
+        if self._h is not None:
+            _abi.lib().insight_b200_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def finalize_sums(op, sums, n_seg, x_dtype, *, fs=1.0, window="hann", nperseg=256,
