@@ -682,7 +682,9 @@ def run_ours(args, w):
                "d2h_bytes_per_step": st["out_bytes"], "ms_per_step": e2e_ms,
                "note": ("per GPU: pinned host input copied in and the whole "
                         "result copied out every step, in channel chunks that "
-                        "overlap the copies with the kernels")}
+                        "overlap the copies with the kernels; bound by the "
+                        "host<->device copies (PCIe, and the host memory that "
+                        "all GPUs of the node share), not by the kernels")}
         del xh, yh, oh
     if "plan" in st:
         st.pop("plan").close()

@@ -76,10 +76,11 @@ __device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
 #ifndef IB200_ACC_MIR
 #define IB200_ACC_MIR 1
 #endif
-// SHF (welch with first-twiddle rows, last radix 2 after a radix-E pass,
-// groups of whole warps: nperseg 8192 in f32 and f64, 512 in f32, 1024 in
-// f64): the last pass runs on warp shuffles (fft_group_w1_lastshfl), one
-// shared-memory exchange and one group barrier fewer per transform.
+// SHF (welch with first-twiddle rows whose transform ends in a radix-2 pass
+// after a radix-E pass, in groups of whole warps; with the shapes chosen in
+// spectral_dispatch.cuh that is f32 nperseg 8192): the last pass runs on warp
+// shuffles (fft_group_w1_lastshfl), one shared-memory exchange and one group
+// barrier fewer per transform.
 #ifndef IB200_ACC_SHFL
 #define IB200_ACC_SHFL 1
 #endif
