@@ -108,6 +108,14 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
     const int g = threadIdx.x / P;
     const int t = threadIdx.x - g * P;
     const V *row = tws + t * TWROW;
+    // first-twiddle rows (TWM 1) are a few values a thread, the same for
+    // every pair: held in registers instead of reread per transform
+    constexpr int NR1 = TWM == 1 ? ThreadTw1<T, L, E>::total() : 1;
+    V row1[NR1];
+    static_for<0, NR1>([&](auto iIC) {
+      constexpr int i = decltype(iIC)::value;
+      row1[i] = TWM == 1 ? row[i] : V{T(1), T(0)};
+    });
     int64_t tile = 0; // tiles of this CTA so far (buffer = tile & 1)
     for (int64_t unit = blockIdx.x; unit < nunits; unit += gridDim.x) {
       const int64_t c = unit / upc;
@@ -162,7 +170,7 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
           if constexpr (TWM == 2)
             fft_group_tw_m<T, L, E, P, GF, 1>(v, buf, GS, t, g, row);
           else if constexpr (TWM == 1)
-            fft_group_w1<T, L, E, P, GF>(v[0], buf, t, g, row);
+            fft_group_w1<T, L, E, P, GF>(v[0], buf, t, g, row1);
           else
             fft_group<T, L, E, P, GF>(v[0], buf, t, g, p.tw);
           if (p.dc_mode == 1 && t == 0)
