@@ -21,9 +21,13 @@ the other workloads ("workloads" in the JSON line):
   istft       the stft workload's complex64 output back to F64 signals
               (GSamples/s of reconstructed samples), channel-sharded
   welch_long  one f32 signal of 2^30 samples, nperseg 8192, 50%, blackman,
-              sharded by segment range over the ranks with one NCCL
-              all-reduce of the F64 partial sums per step; the line carries
-              each rank's partial-sum / all-reduce / finalize times
+              sharded by segment range over the ranks: each rank's F64
+              partial PSD (its segments, averaged with the whole signal's
+              segment count) and one NCCL all-reduce per step; a step
+              replays the rank's kernels as a captured CUDA graph, and the
+              regular call is timed beside it; the line carries each rank's
+              partial / all-reduce times (finalize: no work after the
+              all-reduce)
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload W] [--channels C] [--samples N] [--no-cpu]
@@ -421,11 +425,18 @@ def setup(torch, w, dev, rank, world, stream):
         s0, s1, lo, hi = shard.segment_shard(N, L, L - H, rank, world)
         x = make_long_span(torch, dev, w, lo, hi)
 
-        def step(on_phase=None):
+        def call_step(on_phase=None):
             return shard.welch_segment_sharded(
                 x, N, rank=rank, world=world, fs=w["fs"], window=w["window"],
                 nperseg=L, noverlap=L - H, detrend=w["detrend"], stream=stream,
                 on_phase=on_phase)
+        # the same step with this rank's kernels captured once into a CUDA
+        # graph (the span tensor is fixed); the regular call is timed beside it
+        plan = shard.SegmentShardPlan(
+            x, N, rank=rank, world=world, fs=w["fs"], window=w["window"],
+            nperseg=L, noverlap=L - H, detrend=w["detrend"], stream=stream)
+        step = lambda on_phase=None: plan.run(on_phase=on_phase)
+        st.update(plan=plan, call_step=call_step)
         st.update(step=step, samples_total=N, in_bytes=(hi - lo) * 4,
                   out_bytes=F * 8, transforms=s1 - s0, C_local=1,
                   parallelism=(f"segment-range shards x{world} + one NCCL "
@@ -532,15 +543,21 @@ def timed(torch, R, stream, step, steps, warmup):
     launches0 = ib.launch_count()
     with ClockSampler(R.local) as clk:
         e0.record(stream)
+        h0 = time.perf_counter()
         for _ in range(steps):
             step()
+        h1 = time.perf_counter()
         e1.record(stream)
         torch.cuda.synchronize()
     launches = ib.launch_count() - launches0
     ms_local = e0.elapsed_time(e1) / steps
     ms = R.max(ms_local)
     R.barrier()
-    return ms, ms_local, launches, clk.summary()
+    clocks = clk.summary()
+    # host time to enqueue one step (a step whose device time is not much
+    # above this is bound by the host, not by the kernels)
+    clocks["host_enqueue_ms_per_step"] = (h1 - h0) * 1e3 / steps
+    return ms, ms_local, launches, clocks
 
 
 def phase_breakdown(torch, R, stream, step, steps):
@@ -618,12 +635,16 @@ def measure_extra(torch, R, name, dev, stream, steps, warmup):
            "roofline": roofline_of(w, st, ms_local)}
     res.update(st["detail"])
     if "call_step" in st:
-        cms, _, _, _ = timed(torch, R, stream, st["call_step"], steps, warmup)
-        res["plan"] = ("value and ms_per_step replay the call as a captured CUDA "
-                       "graph (SpectralPlan); ms_per_step_call is the regular call")
+        cms, _, _, cclk = timed(torch, R, stream, st["call_step"], steps, warmup)
+        res["plan"] = ("value and ms_per_step replay this rank's kernels as a "
+                       "captured CUDA graph (SpectralPlan); ms_per_step_call is "
+                       "the regular call")
         res["ms_per_step_call"] = cms
+        res["host_enqueue_ms_per_step_call"] = cclk["host_enqueue_ms_per_step"]
     if name == "welch_long":
         res["breakdown"] = phase_breakdown(torch, R, stream, st["step"], steps)
+        res["breakdown_call"] = phase_breakdown(torch, R, stream, st["call_step"],
+                                                steps)
     if "plan" in st:
         st["plan"].close()
     del st
@@ -658,13 +679,16 @@ def run_ours(args, w):
                                            args.steps, args.warmup)
     value = st["samples_total"] / (ms * 1e-3) / 1e9
     roof = roofline_of(w, st, ms_local)
-    breakdown = None
+    breakdown = breakdown_call = None
     if w["name"] == "welch_long":
         breakdown = phase_breakdown(torch, R, stream, st["step"], args.steps)
-    call_ms = None
+        breakdown_call = phase_breakdown(torch, R, stream, st["call_step"],
+                                         args.steps)
+    call_ms = call_host = None
     if "call_step" in st:
-        call_ms, _, _, _ = timed(torch, R, stream, st["call_step"], args.steps,
-                                 args.warmup)
+        call_ms, _, _, cclk = timed(torch, R, stream, st["call_step"], args.steps,
+                                    args.warmup)
+        call_host = cclk["host_enqueue_ms_per_step"]
 
     # end to end through the public API with pinned host buffers
     e2e = None
@@ -736,11 +760,13 @@ def run_ours(args, w):
         }
         if breakdown is not None:
             line["breakdown"] = breakdown
+            line["breakdown_call"] = breakdown_call
         if call_ms is not None:
-            line["plan"] = ("value and ms_per_step replay the call as a captured "
-                            "CUDA graph (SpectralPlan); ms_per_step_call is the "
-                            "regular call")
+            line["plan"] = ("value and ms_per_step replay this rank's kernels as "
+                            "a captured CUDA graph (SpectralPlan); "
+                            "ms_per_step_call is the regular call")
             line["ms_per_step_call"] = call_ms
+            line["host_enqueue_ms_per_step_call"] = call_host
         if extras:
             line["workloads"] = extras
         print(json.dumps(line), flush=True)

@@ -413,6 +413,12 @@ typedef struct InsightB200SpectralDesc {
   int64_t seg_end;          /* call; seg_end <= 0 -> all segments           */
   int32_t raw_sums;         /* welch/csd: write unscaled F64 sums (for a    */
                             /* cross-device reduction) instead of the PSD   */
+  int64_t avg_segments;     /* welch/csd: average over this many segments   */
+                            /* instead of the call's own count (0 -> own).  */
+                            /* A shard that holds only its segment range of */
+                            /* a longer signal passes the whole signal's    */
+                            /* count: the shards' outputs then sum to the   */
+                            /* PSD, so a plain all-reduce is the last step  */
 } InsightB200SpectralDesc;
 
 /* Output geometry of a call: channels, segments (of the whole signal), bins. */

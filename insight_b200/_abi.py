@@ -98,6 +98,7 @@ class SpectralDesc(ctypes.Structure):
         ("seg_begin", ctypes.c_int64),
         ("seg_end", ctypes.c_int64),
         ("raw_sums", ctypes.c_int32),
+        ("avg_segments", ctypes.c_int64),
     ]
 
 

@@ -114,6 +114,31 @@ __device__ __forceinline__ void static_for(F &&f) {
   }
 }
 
+// Fills entries [0, n) (store(i, load(i))) with `nthreads` threads, each
+// with BATCH independent loads in flight before their stores.  A plain
+// load-then-store loop waits one memory latency per entry, which is what
+// dominates a kernel prologue that fills tables before a short run of work.
+template <int BATCH, typename Ld, typename St>
+__device__ __forceinline__ void fill_batched(int tid, int n, int nthreads,
+                                             Ld &&load, St &&store) {
+  using X = decltype(load(0));
+  for (int i0 = tid; i0 < n; i0 += BATCH * nthreads) {
+    X v[BATCH];
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int i = i0 + q * nthreads;
+      if (i < n)
+        v[q] = load(i);
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int i = i0 + q * nthreads;
+      if (i < n)
+        store(i, v[q]);
+    }
+  }
+}
+
 template <int R> __host__ __device__ constexpr int bitrev(int v) {
   int r = 0;
   for (int m = R >> 1, b = 1; m >= 1; m >>= 1, b <<= 1)
@@ -357,7 +382,7 @@ __device__ __forceinline__ void fill_thread_twiddles(V *tws, const V *tw,
   using PL = Plan<L, E>;
   using TT = ThreadTw<T, L, E>;
   constexpr int NPASS = PL::passes();
-  for (int i = tid; i < P * TT::total(); i += nthreads) {
+  auto load = [&](int i) -> V {
     const int tt = i / TT::total();
     int slot = i - tt * TT::total();
     V val = {T(1), T(0)};
@@ -375,8 +400,12 @@ __device__ __forceinline__ void fill_thread_twiddles(V *tws, const V *tw,
         }
       }
     });
-    tws[tt * TT::stride() + slot] = val;
-  }
+    return val;
+  };
+  fill_batched<8>(tid, P * TT::total(), nthreads, load, [&](int i, V v) {
+    const int tt = i / TT::total();
+    tws[tt * TT::stride() + (i - tt * TT::total())] = v;
+  });
 }
 
 // Per-thread rows of only the first twiddle W^k of every butterfly of the
@@ -451,7 +480,7 @@ __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
   using PL = Plan<L, E>;
   using TT = ThreadTw1<T, L, E>;
   constexpr int NPASS = PL::passes();
-  for (int i = tid; i < P * TT::total(); i += nthreads) {
+  auto load = [&](int i) -> V {
     const int tt = i / TT::total();
     const int slot = i - tt * TT::total();
     V val = {T(1), T(0)};
@@ -474,8 +503,12 @@ __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
         val = tw[k * (L / (NS * R))];
       }
     });
-    rows[tt * TT::stride() + slot] = val;
-  }
+    return val;
+  };
+  fill_batched<8>(tid, P * TT::total(), nthreads, load, [&](int i, V v) {
+    const int tt = i / TT::total();
+    rows[tt * TT::stride() + (i - tt * TT::total())] = v;
+  });
 }
 
 template <typename T, int L, int E, int P, int PASS, typename V>

@@ -582,7 +582,8 @@ C_Status run(const Call &c) {
           d.out_kind = out->dtype == INSIGHT_DTYPE_C32 ? OUT_C64_K : OUT_C128_K;
         }
       }
-      d.avg_scale = scale / (double)S;
+      check(c.avg_segments >= 0, std::string(op) + ": avg_segments must be >= 0");
+      d.avg_scale = scale / (double)(c.avg_segments > 0 ? c.avg_segments : S);
     } else {
       d.kind = LK_STORE;
       // complex: [C?, F, Sl]; F64: [C?, Sl, F] (the reference's transposed view)

@@ -32,6 +32,7 @@ struct Call {
   double scale = 1.0;
   int64_t seg_begin = 0, seg_end = 0;
   bool raw_sums = false;
+  int64_t avg_segments = 0; // welch/csd: averaging count (0 -> the call's own)
   int32_t x_dtype = 0;    // finalize_sums only
   int default_device = 0; // device for CPU inputs
   cudaStream_t stream = nullptr;

@@ -897,6 +897,7 @@ static ib200::Call from_desc(const InsightB200SpectralDesc *d) {
   c.seg_begin = d->seg_begin;
   c.seg_end = d->seg_end;
   c.raw_sums = d->raw_sums != 0;
+  c.avg_segments = d->avg_segments;
   c.default_device = current_device();
   return c;
 }

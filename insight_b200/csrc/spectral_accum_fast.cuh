@@ -136,10 +136,46 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   V *buf2 = buf + (NBUF - 1) * GS;
   T *raw = raws + g * RAWN;
 
-  for (int i = threadIdx.x; i < P * E; i += NT) {
-    const int tt = i / E, e = i - tt * E;
-    wsm[tt * WS + e] = p.win[in_index<L, E, P>(tt, e)];
+  // This CTA's share of the flattened (channel, transform) index space.
+  const int64_t T_all = p.C * p.Tc;
+  const int64_t f0 = flat_start(blockIdx.x, T_all, gridDim.x);
+  const int64_t f1 = flat_start(blockIdx.x + 1, T_all, gridDim.x);
+  const int64_t c_first = f0 / p.Tc;
+
+  // STG: the pair's span [s*step, (s+1)*step + L) when the segments
+  // overlap (b at + step), else a at + 0 and b at + L; x at raw, y at
+  // raw + 2L.
+  auto issue_one = [&](T *dst, const T *src, bool hasb) {
+    if (hasb && p.step < L) {
+      stage_copy<T, P>(dst, src, p.step + L, t);
+    } else {
+      stage_copy<T, P>(dst, src, L, t);
+      if (hasb)
+        stage_copy<T, P>(dst + L, src + p.step, L, t);
+    }
+  };
+  auto issue_c = [&](int64_t c, int64_t task) {
+    const int64_t off = (p.seg0 + 2 * task) * p.step;
+    const bool hasb = (2 * task + 1) < p.S;
+    issue_one(raw, p.x + c * p.x_cs + off, hasb);
+    if constexpr (MODE != ACC_PSD)
+      issue_one(raw + 2 * L, p.y + c * p.y_cs + off, hasb);
+    cp_async_commit();
+  };
+  if constexpr (STG) {
+    // the first task's samples are in flight while the tables are filled
+    if (f0 < f1 && c_first < p.C) {
+      const int64_t task0 = f0 - c_first * p.Tc;
+      const int64_t task1 = min(f1, (c_first + 1) * p.Tc) - c_first * p.Tc;
+      if (task0 + g < task1)
+        issue_c(c_first, task0 + g);
+    }
   }
+
+  fill_batched<8>(
+      threadIdx.x, P * E, NT,
+      [&](int i) { return p.win[in_index<L, E, P>(i / E, i % E)]; },
+      [&](int i, T v) { wsm[(i / E) * WS + i % E] = v; });
   if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   else if constexpr (TWM == 1)
@@ -224,11 +260,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
       v[0] = {T(0), T(0)}; // register 0 of thread 0 holds bin 0
   };
 
-  // This CTA's share of the flattened (channel, transform) index space.
-  const int64_t T_all = p.C * p.Tc;
-  const int64_t f0 = flat_start(blockIdx.x, T_all, gridDim.x);
-  const int64_t f1 = flat_start(blockIdx.x + 1, T_all, gridDim.x);
-  for (int64_t c = f0 / p.Tc; f0 < f1 && c < p.C && c * p.Tc < f1; ++c) {
+  for (int64_t c = c_first; f0 < f1 && c < p.C && c * p.Tc < f1; ++c) {
     const int64_t task0 = max(f0, c * p.Tc) - c * p.Tc;
     const int64_t task1 = min(f1, (c + 1) * p.Tc) - c * p.Tc;
     const int64_t u = blockIdx.x + c; // partial-sum slot of (CTA, channel)
@@ -245,28 +277,10 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
       accf[i] = T(0);
     int nf = 0;
 
-    // STG: the pair's span [s*step, (s+1)*step + L) when the segments
-    // overlap (b at + step), else a at + 0 and b at + L; x at raw, y at
-    // raw + 2L.
-    auto issue_one = [&](T *dst, const T *src, bool hasb) {
-      if (hasb && p.step < L) {
-        stage_copy<T, P>(dst, src, p.step + L, t);
-      } else {
-        stage_copy<T, P>(dst, src, L, t);
-        if (hasb)
-          stage_copy<T, P>(dst + L, src + p.step, L, t);
-      }
-    };
-    auto issue = [&](int64_t task) {
-      const int64_t off = (p.seg0 + 2 * task) * p.step;
-      const bool hasb = (2 * task + 1) < p.S;
-      issue_one(raw, xc + off, hasb);
-      if constexpr (MODE != ACC_PSD)
-        issue_one(raw + 2 * L, yc + off, hasb);
-      cp_async_commit();
-    };
+    auto issue = [&](int64_t task) { issue_c(c, task); };
     if constexpr (STG) {
-      if (task0 + g < task1)
+      // the first channel's first task was requested before the prologue
+      if (c != c_first && task0 + g < task1)
         issue(task0 + g);
     }
 

@@ -171,8 +171,9 @@ __global__ void __launch_bounds__(IstftWsShape<TZ, L, E_>::NT)
   T *wsm = reinterpret_cast<T *>(tws + P * SS::TWS);            // [nperseg]
   fill_thread_w1<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   if constexpr (SS::WSM)
-    for (int i = threadIdx.x; i < p.nperseg; i += NT)
-      wsm[i] = p.win[i];
+    fill_batched<8>(
+        threadIdx.x, (int)p.nperseg, NT, [&](int i) { return p.win[i]; },
+        [&](int i, T v) { wsm[i] = v; });
   __syncthreads();
   const int64_t tpc = (p.Tc + Q - 1) / Q;
   const int64_t ntiles = p.C * tpc;

@@ -406,24 +406,44 @@ template <int MODE>
 __device__ __forceinline__ void finalize_sum(const double *__restrict__ scratch,
                                              int64_t FH, int64_t kk, int64_t q0,
                                              int64_t hi, int64_t dq, double *s) {
-  if (MODE == ACC_COH) {
-    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
-    for (int64_t q = q0; q < hi; q += dq) {
-      const double2 a = s2[2 * (q * FH + kk)];
-      s[0] += a.x;
-      s[1] += a.y;
-      s[2] += s2[2 * (q * FH + kk) + 1].x;
+  // slot values of one bin, read B at a time (independent loads in flight)
+  // and added in slot order, so the sums do not depend on B
+  constexpr int B = 8;
+  auto run = [&](auto ld, auto add) {
+    using X = decltype(ld(int64_t(0)));
+    int64_t q = q0;
+    for (; q + (B - 1) * dq < hi; q += B * dq) {
+      X a[B];
+#pragma unroll
+      for (int j = 0; j < B; ++j)
+        a[j] = ld(q + j * dq);
+#pragma unroll
+      for (int j = 0; j < B; ++j)
+        add(a[j]);
     }
-  } else if (MODE == ACC_PSD) {
-    for (int64_t q = q0; q < hi; q += dq)
-      s[0] += scratch[q * FH + kk];
+    for (; q < hi; q += dq)
+      add(ld(q));
+  };
+  const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
+  if constexpr (MODE == ACC_COH) {
+    run([&](int64_t q) {
+          const double2 a = s2[2 * (q * FH + kk)];
+          return make_double3(a.x, a.y, s2[2 * (q * FH + kk) + 1].x);
+        },
+        [&](double3 a) {
+          s[0] += a.x;
+          s[1] += a.y;
+          s[2] += a.z;
+        });
+  } else if constexpr (MODE == ACC_PSD) {
+    run([&](int64_t q) { return scratch[q * FH + kk]; },
+        [&](double a) { s[0] += a; });
   } else {
-    const double2 *s2 = reinterpret_cast<const double2 *>(scratch);
-    for (int64_t q = q0; q < hi; q += dq) {
-      const double2 v = s2[q * FH + kk];
-      s[0] += v.x;
-      s[1] += v.y;
-    }
+    run([&](int64_t q) { return s2[q * FH + kk]; },
+        [&](double2 a) {
+          s[0] += a.x;
+          s[1] += a.y;
+        });
   }
 }
 
@@ -732,10 +752,10 @@ __global__ void __launch_bounds__(G *(L / E))
   const int t = threadIdx.x - g * P;
   V *buf = smem + g * M * GS; // pairs g*M .. g*M + M - 1
 
-  for (int i = threadIdx.x; i < P * E; i += NT) {
-    const int tt = i / E, e = i - tt * E;
-    wsm[tt * WS + e] = T(0.5) * p.win[in_index<L, E, P>(tt, e)];
-  }
+  fill_batched<8>(
+      threadIdx.x, P * E, NT,
+      [&](int i) { return T(0.5) * p.win[in_index<L, E, P>(i / E, i % E)]; },
+      [&](int i, T v) { wsm[(i / E) * WS + i % E] = v; });
   if constexpr (TWS)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   __syncthreads();

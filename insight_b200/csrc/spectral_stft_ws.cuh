@@ -88,10 +88,10 @@ __global__ void __launch_bounds__(StftWsShape<T, L>::NT)
   V *carry = tws + P * TWROW;                               // [FH][SEC-1]
   T *wsm = reinterpret_cast<T *>(carry + CN);                // [P][WS]
 
-  for (int i = threadIdx.x; i < P * E; i += NT) {
-    const int tt = i / E, e = i - tt * E;
-    wsm[tt * WS + e] = T(0.5) * p.win[in_index<L, E, P>(tt, e)];
-  }
+  fill_batched<8>(
+      threadIdx.x, P * E, NT,
+      [&](int i) { return T(0.5) * p.win[in_index<L, E, P>(i / E, i % E)]; },
+      [&](int i, T v) { wsm[(i / E) * WS + i % E] = v; });
   if constexpr (TWM == 2)
     fill_thread_twiddles<T, L, E, P>(tws, p.tw, threadIdx.x, NT);
   else if constexpr (TWM == 1)

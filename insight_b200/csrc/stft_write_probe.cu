@@ -11,8 +11,9 @@
 // inside [0, S) are written).  Variants:
 //   lsu_v2  NW warps of 8-byte stores (8 lanes per row, 4 rows an instruction)
 //   lsu_v4  NW warps of 16-byte stores (4 lanes per row, 8 rows an instruction)
-//   bulk    NW warps issuing one cp.async.bulk (shared -> this GPU's global
-//           memory, no multicast) of 64 bytes per row run; after each tile
+//   bulk    NW warps issuing one cp.async.bulk (a store-direction copy from
+//           shared memory to this GPU's global memory) of 64 bytes per row
+//           run; after each tile
 //           the issuing threads wait until their copies have read shared
 //           memory (wait_group.read LAG)
 // and a cudaMemsetAsync of the whole output as the contiguous reference.

@@ -6,14 +6,16 @@
 * Segment-range sharding (one very long signal): rank r owns the segments
   [s0, s1) of the whole framing and only the samples they cover,
   [s0*step, (s1-1)*step + nperseg), i.e. its share plus an nperseg - step
-  halo.  Each rank computes unscaled F64 sums over its segments, one
-  all-reduce (sum) over the ranks combines them, and the scale and one-sided
-  mask of the reference csd (src/ops/signal/spectral_analysis.cpp:151-166)
-  are applied once to the reduced sums with the whole signal's segment count.
+  halo.  Each rank sums its segments' spectra in F64 and applies the scale
+  and one-sided mask of the reference csd
+  (src/ops/signal/spectral_analysis.cpp:151-166) with the WHOLE signal's
+  segment count (both are linear), so one all-reduce (sum) over the ranks
+  leaves the PSD itself on every rank: the collective is the last step.
 
-The partial-sum step is a callable so the sharding and reduction logic can
-be exercised on CPU ranks (gloo) with any implementation of it; the default
-runs the B200 kernels.
+The per-rank step is a callable so the sharding and reduction logic can be
+exercised on CPU ranks (gloo) with any implementation of it; the default
+runs the B200 kernels.  A caller may instead return unscaled sums and pass a
+finalize callable that scales the reduced sums.
 """
 from __future__ import annotations
 
@@ -53,26 +55,24 @@ def segment_shard(n_samples: int, nperseg: int, noverlap: int, rank: int,
 
 
 def _gpu_partial(x_span, y_span, *, op, fs, window, nperseg, noverlap, nfft,
-                 detrend, return_onesided, scaling, n_seg_local, stream=None):
+                 detrend, return_onesided, scaling, n_seg_local, n_seg_total,
+                 stream=None):
+    """This rank's share of the result: its segments averaged with the whole
+    signal's count (welch F64; csd complex128 cross spectra)."""
     from . import signal
     code = 1 if op == "csd" else 0
-    _, sums = signal.spectral(code, x_span, y_span, fs=fs, window=window,
+    out = None
+    if op == "csd":
+        import torch
+        F = (int(nfft or nperseg) // 2 + 1) if return_onesided else int(nfft or nperseg)
+        out = torch.empty(F, dtype=torch.complex128, device=x_span.device)
+    _, part = signal.spectral(code, x_span, y_span, fs=fs, window=window,
                               nperseg=nperseg, noverlap=noverlap, nfft=nfft,
                               detrend=detrend, return_onesided=return_onesided,
                               scaling=scaling, seg_range=(0, n_seg_local),
-                              raw_sums=True, stream=stream, axes=False,
-                              sync=stream is None)
-    return sums
-
-
-def _gpu_finalize(sums, *, op, n_seg, x_dtype, fs, window, nperseg, nfft,
-                  return_onesided, scaling, stream=None):
-    from . import signal
-    code = 1 if op == "csd" else 0
-    return signal.finalize_sums(code, sums, n_seg, x_dtype, fs=fs, window=window,
-                                nperseg=nperseg, nfft=nfft,
-                                return_onesided=return_onesided, scaling=scaling,
-                                stream=stream)
+                              avg_segments=n_seg_total, out=out, stream=stream,
+                              axes=False, sync=stream is None)
+    return part
 
 
 def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
@@ -83,17 +83,19 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
                           scaling: str = "density",
                           all_reduce: Optional[Callable] = None,
                           partial: Callable = _gpu_partial,
-                          finalize: Callable = _gpu_finalize, stream=None,
+                          finalize: Optional[Callable] = None, stream=None,
                           on_phase: Optional[Callable[[str], None]] = None):
     """Welch PSD (or csd) of one long signal sharded by segment range.
 
     x_span (and y_span) hold this rank's samples [lo, hi) of
     segment_shard(n_samples, nperseg, noverlap, rank, world).  Returns the
     reduced, scaled result on every rank.  all_reduce(tensor) sums in place
-    over the ranks (torch.distributed.all_reduce by default).  on_phase(name),
-    when given, is called after each of the three steps has been enqueued
-    ("partial", "all_reduce", "finalize"), e.g. to record a CUDA event on
-    the stream between them.
+    over the ranks (torch.distributed.all_reduce by default).  partial(...)
+    returns this rank's share, already averaged over n_seg_total segments,
+    unless a finalize(sums, ...) callable is given to scale the reduced sums.
+    on_phase(name), when given, is called after each step has been enqueued
+    ("partial", "all_reduce", and "finalize" even when there is none), e.g.
+    to record a CUDA event on the stream between them.
     """
     step, S = framing(n_samples, nperseg, noverlap)
     s0, s1, lo, hi = segment_shard(n_samples, nperseg, noverlap, rank, world)
@@ -103,7 +105,7 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
               nfft=nfft, detrend=detrend, return_onesided=return_onesided,
               scaling=scaling)
     sums = partial(x_span, y_span if op == "csd" else None, n_seg_local=s1 - s0,
-                   stream=stream, **kw)
+                   n_seg_total=S, stream=stream, **kw)
     if on_phase is not None:
         on_phase("partial")
     if all_reduce is None:
@@ -119,10 +121,68 @@ def welch_segment_sharded(x_span, n_samples: int, *, rank: int, world: int,
             all_reduce(sums)
     if on_phase is not None:
         on_phase("all_reduce")
-    x_dtype = str(x_span.dtype)
-    res = finalize(sums, op=op, n_seg=S, x_dtype=x_dtype, fs=fs, window=window,
-                   nperseg=nperseg, nfft=nfft, return_onesided=return_onesided,
-                   scaling=scaling, stream=stream)
+    res = sums
+    if finalize is not None:
+        res = finalize(sums, op=op, n_seg=S, x_dtype=str(x_span.dtype), fs=fs,
+                       window=window, nperseg=nperseg, nfft=nfft,
+                       return_onesided=return_onesided, scaling=scaling,
+                       stream=stream)
     if on_phase is not None:
         on_phase("finalize")
     return res
+
+
+class SegmentShardPlan:
+    """welch_segment_sharded for repeated calls on the same span tensors (a
+    signal buffer refilled in place between calls): this rank's step (the
+    accumulate kernel and the slot fold, averaged with the whole signal's
+    segment count) is captured once into a CUDA graph (signal.SpectralPlan),
+    so a call is one graph launch plus the all-reduce.  run() returns the
+    reduced result (the same tensor every call)."""
+
+    def __init__(self, x_span, n_samples: int, *, rank: int, world: int,
+                 y_span=None, op: str = "welch", fs: float = 1.0,
+                 window: str = "hann", nperseg: int = 256, noverlap: int = 0,
+                 nfft: int = 0, detrend: str = "constant",
+                 return_onesided: bool = True, scaling: str = "density",
+                 stream=None):
+        import torch
+
+        from . import signal
+        _, S = framing(n_samples, nperseg, noverlap)
+        s0, s1, lo, hi = segment_shard(n_samples, nperseg, noverlap, rank, world)
+        if len(x_span) != hi - lo:
+            raise ValueError(f"rank {rank}: expected {hi - lo} samples, "
+                             f"got {len(x_span)}")
+        n = int(nfft or nperseg)
+        F = n // 2 + 1 if return_onesided else n
+        csd = op == "csd"
+        self.out = torch.empty(F, dtype=torch.complex128 if csd else torch.float64,
+                               device=x_span.device)
+        self.world, self.stream = world, stream
+        self._plan = signal.SpectralPlan(
+            signal._abi.OP_CSD if csd else signal._abi.OP_WELCH, x_span,
+            y_span if csd else None, out=self.out, fs=fs, window=window,
+            nperseg=nperseg, noverlap=noverlap, nfft=nfft, detrend=detrend,
+            return_onesided=return_onesided, scaling=scaling,
+            seg_range=(0, s1 - s0), avg_segments=S, stream=stream)
+
+    def run(self, all_reduce: Optional[Callable] = None,
+            on_phase: Optional[Callable[[str], None]] = None):
+        self._plan.run(stream=self.stream)
+        if on_phase is not None:
+            on_phase("partial")
+        if self.world > 1:
+            if all_reduce is None:
+                import torch.distributed as dist
+                all_reduce = dist.all_reduce
+            import torch
+            with torch.cuda.stream(self.stream):
+                all_reduce(self.out)
+        if on_phase is not None:
+            on_phase("all_reduce")
+            on_phase("finalize")
+        return self.out
+
+    def close(self):
+        self._plan.close()

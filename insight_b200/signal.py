@@ -87,11 +87,12 @@ _DESC_CACHE: dict = {}
 
 
 def _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
-          scaling="density", mode="psd", axis=-1, seg_range=None, raw_sums=False):
+          scaling="density", mode="psd", axis=-1, seg_range=None, raw_sums=False,
+          avg_segments=0):
     """The call descriptor; repeated calls with the same arguments reuse one
     (the backend only reads it)."""
     key = (op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
-           scaling, mode, axis, seg_range, raw_sums)
+           scaling, mode, axis, seg_range, raw_sums, int(avg_segments or 0))
     d = _DESC_CACHE.get(key)
     if d is None:
         if len(_DESC_CACHE) >= 256:
@@ -101,7 +102,7 @@ def _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
 
 
 def _make_desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
-               scaling, mode, axis, seg_range, raw_sums):
+               scaling, mode, axis, seg_range, raw_sums, avg_segments):
     d = _abi.SpectralDesc()
     d.op = op
     d.axis = axis
@@ -116,6 +117,7 @@ def _make_desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided
     d.mode = mode.encode()
     d.seg_begin, d.seg_end = (seg_range if seg_range is not None else (0, 0))
     d.raw_sums = 1 if raw_sums else 0
+    d.avg_segments = int(avg_segments)
     return d
 
 
@@ -135,8 +137,8 @@ def spectral_shape(op, x, nperseg=256, noverlap=None, nfft=None,
 def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None,
              nfft=None, detrend="constant", return_onesided=True,
              scaling="density", mode="psd", axis=-1, complex_output=False,
-             seg_range=None, raw_sums=False, out=None, stream=None, sync=True,
-             axes=True):
+             seg_range=None, raw_sums=False, avg_segments=0, out=None, stream=None,
+             sync=True, axes=True):
     """Native batched entry point (insight_b200_spectral).
 
     Returns ``(f, out)`` for welch/csd and ``(f, t, out)`` for
@@ -145,9 +147,13 @@ def spectral(op, x, y=None, *, fs=1.0, window="hann", nperseg=256, noverlap=None
     F64 / complex128); spectrogram/stft F64 ``[C, S, F]`` (the reference's
     (n_seg, n_freq) orientation) or complex ``[C, F, S]`` with
     ``complex_output``.  1-D inputs drop the leading channel axis.
+    ``avg_segments`` (welch/csd) averages over that many segments instead of
+    the call's own count: a shard holding one segment range of a longer
+    signal passes the whole signal's count, and the shards' outputs sum to
+    the PSD.
     """
     d = _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
-              scaling, mode, axis, seg_range, raw_sums)
+              scaling, mode, axis, seg_range, raw_sums, avg_segments)
     xa = _abi.as_array(x)
     ya = _abi.as_array(y) if y is not None else None
     if out is None or axes:
@@ -208,10 +214,10 @@ class SpectralPlan:
     def __init__(self, op, x, y=None, *, out, fs=1.0, window="hann", nperseg=256,
                  noverlap=None, nfft=None, detrend="constant", return_onesided=True,
                  scaling="density", mode="psd", axis=-1, seg_range=None,
-                 raw_sums=False, stream=None):
+                 raw_sums=False, avg_segments=0, stream=None):
         self._h = None
         d = _desc(op, fs, window, nperseg, noverlap, nfft, detrend, return_onesided,
-                  scaling, mode, axis, seg_range, raw_sums)
+                  scaling, mode, axis, seg_range, raw_sums, avg_segments)
         xa, ya, oa = _abi.as_array(x), _abi.as_array(y), _abi.as_array(out)
         h = ctypes.c_void_p()
         _abi.check(_abi.lib().insight_b200_plan_create(

@@ -121,8 +121,11 @@ def test_config_5_long_welch_and_segment_shards(g, cuda):
     r = ib.welch(x, **kw)
     assert np.array_equal(_np(r.f), g["config_5/f"])
     assert so.max_rel_err(_np(r.Pxx), g["config_5/Pxx"]) <= 1e-5
-    # four segment-range shards, raw sums reduced on the host
+    # four segment-range shards, each given only its sample span and scaled
+    # with the whole signal's segment count; their sum (what the all-reduce
+    # forms) is the PSD
     W, n = 4, len(xh)
+    _, S = shard.framing(n, kw["nperseg"], kw["noverlap"])
     parts = []
     for rank in range(W):
         s0, s1, lo, hi = shard.segment_shard(n, kw["nperseg"], kw["noverlap"],
@@ -131,11 +134,6 @@ def test_config_5_long_welch_and_segment_shards(g, cuda):
             x[lo:hi], None, op="welch", fs=kw["fs"], window=kw["window"],
             nperseg=kw["nperseg"], noverlap=kw["noverlap"], nfft=0,
             detrend=kw["detrend"], return_onesided=True, scaling="density",
-            n_seg_local=s1 - s0))
-    sums = sum(parts)
-    _, S = shard.framing(n, kw["nperseg"], kw["noverlap"])
-    out = shard._gpu_finalize(sums, op="welch", n_seg=S, x_dtype="float32",
-                              fs=kw["fs"], window=kw["window"],
-                              nperseg=kw["nperseg"], nfft=0, return_onesided=True,
-                              scaling="density")
+            n_seg_local=s1 - s0, n_seg_total=S))
+    out = sum(parts)
     assert so.max_rel_err(_np(out), g["config_5/Pxx"]) <= 1e-5

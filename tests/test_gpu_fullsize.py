@@ -237,12 +237,14 @@ def test_welch_long_full_size_and_segment_shards(cuda):
     one = ib.welch(x, **kw).Pxx
 
     W = 8
+    _, S_all = shard.framing(N, L, L - H)
     parts = []
     for rk in range(W):
         s0, s1, lo, hi = shard.segment_shard(N, L, L - H, rk, W)
         parts.append(shard._gpu_partial(x[lo:hi], None, op="welch", nfft=0,
                                         return_onesided=True, scaling="density",
-                                        n_seg_local=s1 - s0, **kw))
+                                        n_seg_local=s1 - s0, n_seg_total=S_all,
+                                        **kw))
     total = torch.stack(parts).sum(dim=0)
 
     def _sum_all(t):

@@ -501,6 +501,42 @@ def test_storage_offset_view(cuda):
 
 # ---------------------------------------------- segment-range shards + sums ----
 @pytest.mark.parametrize("op", ["welch", "csd"])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_span_shards_scaled_with_the_whole_count(cuda, op, dtype):
+    """Each shard holds only its samples and averages over the whole signal's
+    segment count (avg_segments): the shards' outputs sum to the PSD."""
+    import torch
+    from insight_b200 import shard
+    L, ov, n = 256, 96, 40 * 256 + 77
+    x = _sig(n, dtype, 31)
+    y = _sig(n, dtype, 32)
+    step, S = shard.framing(n, L, ov)
+    code = ib.OP_WELCH if op == "welch" else ib.OP_CSD
+    F = L // 2 + 1
+    total = None
+    for k in range(3):
+        s0, s1, lo, hi = shard.segment_shard(n, L, ov, k, 3)
+        out = torch.empty(F, dtype=torch.complex128, device=cuda) if op == "csd" else None
+        _, part = ib.spectral(code, _to_gpu(x[lo:hi], cuda),
+                              _to_gpu(y[lo:hi], cuda) if op == "csd" else None,
+                              fs=3.0, window="hamming", nperseg=L, noverlap=ov,
+                              seg_range=(0, s1 - s0), avg_segments=S, out=out)
+        total = part if total is None else total + part
+    torch.cuda.synchronize()
+    if op == "welch":
+        _, ref = so.welch(x, fs=3.0, window="hamming", nperseg=L, noverlap=ov)
+    else:
+        _, ref = so.csd(x, y, fs=3.0, window="hamming", nperseg=L, noverlap=ov,
+                        complex_output=True)
+    tol = 1e-5 if dtype == np.float32 else 1e-12
+    assert so.max_rel_err(total.cpu().numpy(), ref) <= tol
+
+
+def test_avg_segments_rejects_negative(cuda):
+    with pytest.raises(RuntimeError, match="avg_segments"):
+        ib.spectral(ib.OP_WELCH, _to_gpu(_sig(4096, np.float64, 3), cuda),
+                    nperseg=256, avg_segments=-1)
+@pytest.mark.parametrize("op", ["welch", "csd"])
 @pytest.mark.parametrize("shards", [2, 3])
 def test_segment_range_sums(cuda, op, shards):
     import torch

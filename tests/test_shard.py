@@ -1,9 +1,10 @@
 """Host-side multi-rank logic of insight_b200.shard, on CPU ranks (gloo).
 
-The per-rank partial sums come from the CPU oracle so the test needs no GPU;
-what is tested is the sharding (segment ranges, sample spans with halo,
-channel blocks), the cross-rank sum through torch.distributed, and the final
-scale / one-sided mask applied with the whole signal's segment count.
+The per-rank steps come from the CPU oracle so the test needs no GPU; what
+is tested is the sharding (segment ranges, sample spans with halo, channel
+blocks), the cross-rank sum through torch.distributed, and the scale /
+one-sided mask with the whole signal's segment count: applied by each rank
+before the all-reduce (the default), or once to the reduced raw sums.
 """
 import os
 import socket
@@ -20,7 +21,8 @@ from oracle import spectral_oracle as so
 
 
 def _oracle_partial(x_span, y_span, *, op, fs, window, nperseg, noverlap, nfft,
-                    detrend, return_onesided, scaling, n_seg_local, stream=None):
+                    detrend, return_onesided, scaling, n_seg_local, n_seg_total,
+                    stream=None):
     x = x_span.numpy()
     y = y_span.numpy() if y_span is not None else x
     sums, n_seg = so.csd_sums(x, y if op == "csd" else x, nperseg, noverlap, nfft,
@@ -41,13 +43,28 @@ def _oracle_finalize(sums, *, op, n_seg, x_dtype, fs, window, nperseg, nfft,
     return sums * torch.from_numpy(f)
 
 
+def _oracle_share(x_span, y_span, *, op, fs, window, nperseg, noverlap, nfft,
+                  detrend, return_onesided, scaling, n_seg_local, n_seg_total,
+                  stream=None):
+    """This rank's sums scaled with the whole signal's segment count (the
+    default GPU step's contract): the shares sum to the result."""
+    sums = _oracle_partial(x_span, y_span, op=op, fs=fs, window=window,
+                           nperseg=nperseg, noverlap=noverlap, nfft=nfft,
+                           detrend=detrend, return_onesided=return_onesided,
+                           scaling=scaling, n_seg_local=n_seg_local,
+                           n_seg_total=n_seg_total)
+    return _oracle_finalize(sums, op=op, n_seg=n_seg_total, x_dtype="float64",
+                            fs=fs, window=window, nperseg=nperseg, nfft=nfft,
+                            return_onesided=return_onesided, scaling=scaling)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path, op, kw):
+def _worker(rank, world, port, out_path, op, kw, prescaled):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -63,22 +80,24 @@ def _worker(rank, world, port, out_path, op, kw):
             y_span=torch.from_numpy(y[lo:hi].copy()), op=op, fs=kw["fs"],
             window=kw["window"], nperseg=kw["nperseg"], noverlap=kw["noverlap"],
             detrend=kw["detrend"], all_reduce=dist.all_reduce,
-            partial=_oracle_partial, finalize=_oracle_finalize)
+            partial=_oracle_share if prescaled else _oracle_partial,
+            finalize=None if prescaled else _oracle_finalize)
         if rank == 0:
             np.save(out_path, res.numpy())
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("prescaled", [True, False])
 @pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("op", ["welch", "csd"])
-def test_segment_sharded_reduction(world, op):
+def test_segment_sharded_reduction(world, op, prescaled):
     kw = dict(n=50_000, fs=7.0, window="hamming", nperseg=512, noverlap=0,
               detrend="constant")
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "res.npy")
-        mp.spawn(_worker, args=(world, _free_port(), out, op, kw), nprocs=world,
-                 join=True)
+        mp.spawn(_worker, args=(world, _free_port(), out, op, kw, prescaled),
+                 nprocs=world, join=True)
         got = np.load(out)
     rng = np.random.default_rng(42)
     x = rng.standard_normal(kw["n"])
