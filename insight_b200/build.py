@@ -29,6 +29,7 @@ CU_SOURCES = ["spectral_f32.cu", "spectral_f64.cu", "spectral_util.cu",
 CPP_SOURCES = ["launch.cpp", "frontend.cpp", "plugin.cpp", "windows.cpp"]
 HEADERS = ["fft_core.cuh", "spectral_kernels.cuh", "spectral_dispatch.cuh",
            "spectral_accum_fast.cuh", "spectral_istft.cuh", "spectral_stft_ws.cuh",
+           "spectral_stft_tma.cuh",
            "launch.h", "frontend.h", "windows.h"]
 
 

@@ -5,8 +5,11 @@
 #include "spectral_kernels.cuh"
 #include "spectral_accum_fast.cuh"
 #include "spectral_stft_ws.cuh"
+#include "spectral_stft_tma.cuh"
 
+#include <cudaTypedefs.h>
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 namespace ib200 {
@@ -276,9 +279,122 @@ cudaError_t run_stft_ws_sh(const LaunchDesc &d, int num_sms, cudaStream_t stream
   return cudaGetLastError();
 }
 
+// TMA-store variant (spectral_stft_tma.cuh): f32, nperseg = nfft = 2048,
+// contiguous bin rows, 32-byte-aligned output.
+#ifndef IB200_STFT_TMA
+#define IB200_STFT_TMA 1
+#endif
+
+// cuTensorMapEncodeTiled from the driver, looked up once per process.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault,
+                                &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+inline bool stft_tma_eligible(const LaunchDesc &d) {
+  return IB200_STFT_TMA && !d.f64 && d.nfft == StftTma::L && d.S >= 1 &&
+         d.C >= 1 && d.o_ts == 1 && d.o_rs >= d.S &&
+         d.o_cs == StftTma::F * d.o_rs &&
+         (reinterpret_cast<uintptr_t>(d.out) & 31) == 0 &&
+         d.C * StftTma::F / 4 + StftTma::ROWS < (int64_t(1) << 31) &&
+         2 * (d.S + 4) < (int64_t(1) << 31) &&
+         32 * d.o_rs < (int64_t(1) << 40) && tensor_map_encoder() != nullptr;
+}
+
+// Tensor map of the rows R = c*F + k with R mod 4 == m: their sector-aligned
+// origin (d_m = (m * o_rs) mod 4 elements before row m's first column), a
+// stride of 4 rows, S + d_m complex columns as 2 (S + d_m) floats, boxes of
+// 8 columns x 256 rows with the 64-byte swizzle.
+inline cudaError_t encode_stft_map(CUtensorMap *tm, const LaunchDesc &d, int m) {
+  const int64_t dm = (m * (d.o_rs & 3)) & 3;
+  float2 *base = reinterpret_cast<float2 *>(d.out) + (m * d.o_rs - dm);
+  const cuuint64_t dims[2] = {(cuuint64_t)(2 * (d.S + dm)),
+                              (cuuint64_t)((d.C * StftTma::F - m + 3) / 4)};
+  const cuuint64_t strides[1] = {(cuuint64_t)(32 * d.o_rs)};
+  const cuuint32_t box[2] = {2 * StftTma::W, StftTma::ROWS};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tensor_map_encoder()(
+      tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int SH, bool TW>
+cudaError_t run_stft_tma_sh(const LaunchDesc &d, int num_sms, cudaStream_t stream,
+                            int64_t *launches) {
+  using K = StftTma;
+  auto kern = stft_tma_kernel<SH, TW>;
+  static const cudaError_t attr = cudaFuncSetAttribute(
+      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::SMEM);
+  if (attr != cudaSuccess)
+    return attr;
+  StftTmaArgs a{};
+  a.x = reinterpret_cast<const float *>(d.x);
+  a.x_cs = d.x_cs;
+  a.step = d.step;
+  a.seg0 = d.seg0;
+  a.S = d.S;
+  a.tpc = ((d.S + 1) / 2 + K::Q - 1) / K::Q;
+  a.ntiles = d.C * a.tpc;
+  a.win = reinterpret_cast<const float *>(d.win);
+  a.tw = reinterpret_cast<const float2 *>(d.tw);
+  a.out = reinterpret_cast<float2 *>(d.out);
+  a.o_cs = d.o_cs;
+  a.o_rs = d.o_rs;
+  a.dc_mode = d.dc_mode;
+  CUtensorMap tm[4];
+  for (int m = 0; m < 4; ++m) {
+    cudaError_t e = encode_stft_map(&tm[m], d, m);
+    if (e != cudaSuccess)
+      return e;
+  }
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.ntiles, num_sms));
+  kern<<<(unsigned)grid, K::nt(TW), K::SMEM, stream>>>(a, tm[0], tm[1], tm[2], tm[3]);
+  if (launches)
+    *launches += 1;
+  return cudaGetLastError();
+}
+
+template <bool TW>
+cudaError_t run_stft_tma(const LaunchDesc &d, int num_sms, cudaStream_t stream,
+                         int64_t *launches) {
+  const int sh = fast_shift<float, StftTma::L>(d.step);
+  if (sh == 4)
+    return run_stft_tma_sh<4, TW>(d, num_sms, stream, launches);
+  if (sh == 8)
+    return run_stft_tma_sh<8, TW>(d, num_sms, stream, launches);
+  return run_stft_tma_sh<0, TW>(d, num_sms, stream, launches);
+}
+
+// EXPERIMENT: IB200_STFT_VARIANT=ws|tw|t0 (default t0)
+inline int stft_variant() {
+  static const int v = [] {
+    const char *e = getenv("IB200_STFT_VARIANT");
+    if (!e) return 2;
+    if (e[0] == 'w') return 0;
+    if (e[0] == 't' && e[1] == 'w') return 1;
+    return 2;
+  }();
+  return v;
+}
+
 template <typename T, int L>
 cudaError_t run_stft_fast(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                           int64_t *launches) {
+  if constexpr (std::is_same<T, float>::value && L == StftTma::L) {
+    if (stft_tma_eligible(d) && stft_variant() != 0)
+      return stft_variant() == 1 ? run_stft_tma<true>(d, num_sms, stream, launches)
+                                 : run_stft_tma<false>(d, num_sms, stream, launches);
+  }
   if constexpr (stft_ws_mode<T, L>() > 0) {
     constexpr int E = values_per_thread<T>(L);
     constexpr int R0 = Plan<L, E>::radix(0);
