@@ -306,6 +306,7 @@ inline bool stft_tma_eligible(const LaunchDesc &d) {
          (reinterpret_cast<uintptr_t>(d.out) & 31) == 0 &&
          d.C * StftTma::F / 4 + StftTma::ROWS < (int64_t(1) << 31) &&
          2 * (d.S + 4) < (int64_t(1) << 31) &&
+         d.C * ((d.S + 1) / 2 / StftTma::Q + 1) < (int64_t(1) << 31) &&
          32 * d.o_rs < (int64_t(1) << 40) && tensor_map_encoder() != nullptr;
 }
 
@@ -342,9 +343,9 @@ cudaError_t run_stft_tma_sh(const LaunchDesc &d, int num_sms, cudaStream_t strea
   a.x_cs = d.x_cs;
   a.step = d.step;
   a.seg0 = d.seg0;
-  a.S = d.S;
-  a.tpc = ((d.S + 1) / 2 + K::Q - 1) / K::Q;
-  a.ntiles = d.C * a.tpc;
+  a.S = (int)d.S;
+  a.tpc = (int)(((d.S + 1) / 2 + K::Q - 1) / K::Q);
+  a.ntiles = (int)(d.C * a.tpc);
   a.win = reinterpret_cast<const float *>(d.win);
   a.tw = reinterpret_cast<const float2 *>(d.tw);
   a.out = reinterpret_cast<float2 *>(d.out);

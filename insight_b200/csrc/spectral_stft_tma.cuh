@@ -75,9 +75,9 @@ struct StftTma {
 struct StftTmaArgs {
   const float *x;       // channel 0, sample 0
   int64_t x_cs, step, seg0;
-  int64_t S;            // segments (columns) per channel
-  int64_t tpc;          // tiles per channel
-  int64_t ntiles;       // C * tpc
+  int S;                // segments (columns) per channel
+  int tpc;              // tiles per channel
+  int ntiles;           // C * tpc
   const float *win;     // [2048]
   const float2 *tw;     // [2048], W_2048^m
   float2 *out;          // element (c, k, s) at out[c*o_cs + k*o_rs + s]
@@ -105,13 +105,13 @@ __device__ __forceinline__ void tma_store_box(const CUtensorMap *m, uint32_t src
 // none at a channel's last tile.  Every box lies inside its rows.
 __device__ __forceinline__ void issue_boxes(
     const CUtensorMap *tm0, const CUtensorMap *tm1, const CUtensorMap *tm2,
-    const CUtensorMap *tm3, uint32_t stg_s, int64_t c, int64_t tl, int64_t tpc,
-    bool first, int orp) {
+    const CUtensorMap *tm3, uint32_t stg_s, int c, int tl, int tpc, bool first,
+    int orp) {
   if (tl + 1 == tpc)
     return; // stored directly (see the writers)
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const int64_t R = c * StftTma::F + q;
+    const int64_t R = (int64_t)c * StftTma::F + q;
     const int m = (int)(R & 3);
     const int d = (m * orp) & 3;
     if (first && d != 0)
@@ -143,16 +143,16 @@ __global__ void __launch_bounds__(StftTma::nt(TW), 1)
   V *car = reinterpret_cast<V *>(stg + K::STG + K::XCH);     // [4][256][3]
   const uint32_t stg_s = sraw + pad;
 
-  const int64_t fb = (int64_t)blockIdx.x * p.ntiles / gridDim.x;
-  const int64_t fe = (int64_t)(blockIdx.x + 1) * p.ntiles / gridDim.x;
+  const int fb = (int)((int64_t)blockIdx.x * p.ntiles / gridDim.x);
+  const int fe = (int)((int64_t)(blockIdx.x + 1) * p.ntiles / gridDim.x);
   const int orp = (int)(p.o_rs & 3);
   constexpr int NT = K::nt(TW);
 
   if (TW && threadIdx.x >= K::NFT) {
     // ------------------------------------------------------------ TMA warp
     const bool lead = threadIdx.x == K::NFT;
-    int64_t c = fb / p.tpc, tl = fb - c * p.tpc;
-    for (int64_t f = fb; f < fe; ++f) {
+    int c = fb / p.tpc, tl = fb - c * p.tpc;
+    for (int f = fb; f < fe; ++f) {
       const bool first = f == fb || tl == 0;
       named_sync(K::FULL, NT);
       if (lead) {
@@ -196,40 +196,59 @@ __global__ void __launch_bounds__(StftTma::nt(TW), 1)
   const V twb = p.tw[jb1];
 
   float nx[E + NB]; // this tile's samples: segment a, then b's own
-  auto load_tile = [&](int64_t c, int64_t tl) {
-    const int64_t task = tl * K::Q + g;
-    const bool va = 2 * task < p.S, vb = 2 * task + 1 < p.S;
-    const float *xa = p.x + c * p.x_cs + (p.seg0 + 2 * task) * p.step + t;
-    static_for<0, E>([&](auto eIC) {
-      constexpr int e = decltype(eIC)::value;
-      nx[e] = va ? __ldg(xa + P * e) : 0.f;
-    });
-    static_for<0, NB>([&](auto eIC) {
-      constexpr int e = decltype(eIC)::value;
-      nx[E + e] = vb ? __ldg(xa + p.step + P * (E - NB + e)) : 0.f;
-    });
+  // both segments of the pair exist (all but a channel's last pair or two)
+  auto full_pair = [&](int tl) { return 2 * (tl * K::Q + g) + 1 < p.S; };
+  auto load_tile = [&](int c, int tl) {
+    const int task = tl * K::Q + g;
+    const float *xa = p.x + c * p.x_cs + (p.seg0 + 2 * (int64_t)task) * p.step + t;
+    if (full_pair(tl)) {
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        nx[e] = __ldg(xa + P * e);
+      });
+      static_for<0, NB>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        nx[E + e] = __ldg(xa + p.step + P * (E - NB + e));
+      });
+    } else { // segment b (and maybe a) past the channel's last segment
+      const bool va = 2 * task < p.S;
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        nx[e] = va ? __ldg(xa + P * e) : 0.f;
+      });
+      static_for<0, NB>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        nx[E + e] = 0.f;
+      });
+    }
   };
 
-  int64_t c = fb / p.tpc, tl = fb - c * p.tpc;
+  int c = fb / p.tpc, tl = fb - c * p.tpc;
   if (fb < fe)
     load_tile(c, tl);
-  for (int64_t f = fb; f < fe; ++f) {
+  for (int f = fb; f < fe; ++f) {
     const bool first = f == fb || tl == 0;
     const bool last = f + 1 == fe || tl + 1 == p.tpc;
-    const int64_t x0 = tl * K::W;
-    const bool vb = 2 * (tl * K::Q + g) + 1 < p.S;
+    const int x0 = tl * K::W;
     V v[E];
-    static_for<0, E>([&](auto eIC) {
-      constexpr int e = decltype(eIC)::value;
-      float b;
-      if constexpr (SH > 0 && e + SH < E)
-        b = nx[e + SH];
-      else
-        b = nx[E + e - (E - NB)];
-      v[e] = {nx[e] * wv[e], (vb ? b : 0.f) * wv[e]};
-    });
+    if (full_pair(tl)) {
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        float b;
+        if constexpr (SH > 0 && e + SH < E)
+          b = nx[e + SH];
+        else
+          b = nx[E + e - (E - NB)];
+        v[e] = {nx[e] * wv[e], b * wv[e]};
+      });
+    } else { // segment b is zero
+      static_for<0, E>([&](auto eIC) {
+        constexpr int e = decltype(eIC)::value;
+        v[e] = {nx[e] * wv[e], 0.f};
+      });
+    }
     // next tile of this run
-    int64_t cn = c, tn = tl + 1;
+    int cn = c, tn = tl + 1;
     if (tn == p.tpc) {
       tn = 0;
       ++cn;
@@ -288,82 +307,143 @@ __global__ void __launch_bounds__(StftTma::nt(TW), 1)
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       named_sync(K::EMPTY, NT);
     }
-    V *outc = p.out + c * p.o_cs + x0 + 2 * g;
-    const bool okA = x0 + 2 * g < p.S, okB = x0 + 2 * g + 1 < p.S;
-    const int64_t R0 = c * F;
-    const bool nobox = tl + 1 == p.tpc; // a channel's last tile: no boxes
-    // one bin (class q, row i, bin k) of this thread's two columns
-    auto put = [&](int q, V *cr, int i, int k, V A, V B) {
-      const int d = (int)((((R0 + q) & 3) * orp) & 3);
-      const int sA = 2 * g + d; // staging column of A (B at sA + 1)
-      V *gp = outc + (int64_t)k * p.o_rs;
-      const bool dir = nobox || (first && d != 0);
-      if (sA + 1 < K::W) {
-        if (dir) {
-          if (okA)
-            gp[0] = A;
-          if (okB)
-            gp[1] = B;
-        } else if ((sA & 1) == 0) {
-          *reinterpret_cast<float4 *>(stg + stma_off(q, i, sA)) =
-              make_float4(A.x, A.y, B.x, B.y);
-        } else {
-          *reinterpret_cast<V *>(stg + stma_off(q, i, sA)) = A;
-          *reinterpret_cast<V *>(stg + stma_off(q, i, sA + 1)) = B;
-        }
-      } else if (sA < K::W) { // B is carried (slot 0)
-        if (dir) {
-          if (okA)
-            gp[0] = A;
-        } else {
-          *reinterpret_cast<V *>(stg + stma_off(q, i, sA)) = A;
-        }
-        if (!first) { // the previous tile's B of this thread
-          if (nobox)
-            gp[1 - K::W] = cr[i * 3];
-          else
-            *reinterpret_cast<V *>(stg + stma_off(q, i, 0)) = cr[i * 3];
-        }
-        if (last) {
-          if (okB)
-            gp[1] = B;
-        } else {
-          cr[i * 3] = B;
-        }
-      } else { // both carried (slots sA - 8, sA - 7)
-        const int s0 = sA - K::W;
-        if (!first) {
-          if (nobox) {
-            gp[-K::W] = cr[i * 3 + s0];
-            gp[1 - K::W] = cr[i * 3 + s0 + 1];
+    // phase of class q's rows in this channel: ((c*F + q) * o_rs) mod 4
+    const int cf4 = (int)(((int64_t)c * F) & 3);
+    const int d1 = (((cf4 + q1) & 3) * orp) & 3;
+    const int d2 = (((cf4 + q2) & 3) * orp) & 3;
+    if (!first && !last) {
+      // ------------------------------------------- common tile: staging only
+      // class q, rows i + 64 r: byte offsets rb + 4096 r; carry slots
+      // cr[i*3 + s] + 192 r
+      auto stage = [&](int q, int i, V *cr, int d, const V *A, const V *B) {
+        const int sA = 2 * g + d;
+        const int rb = q * K::BOX_BYTES + i * 64;
+        const int sw = ((i >> 1) & 3) << 4;
+        V *c0 = cr + i * 3;
+        if (sA + 1 < K::W) {
+          const int oA = rb + ((8 * sA) ^ sw);
+          if ((sA & 1) == 0) {
+            static_for<0, 4>([&](auto rIC) {
+              constexpr int r = decltype(rIC)::value;
+              *reinterpret_cast<float4 *>(stg + oA + 4096 * r) =
+                  make_float4(A[r].x, A[r].y, B[r].x, B[r].y);
+            });
           } else {
-            *reinterpret_cast<V *>(stg + stma_off(q, i, s0)) = cr[i * 3 + s0];
-            *reinterpret_cast<V *>(stg + stma_off(q, i, s0 + 1)) = cr[i * 3 + s0 + 1];
+            const int oB = rb + ((8 * sA + 8) ^ sw);
+            static_for<0, 4>([&](auto rIC) {
+              constexpr int r = decltype(rIC)::value;
+              *reinterpret_cast<V *>(stg + oA + 4096 * r) = A[r];
+              *reinterpret_cast<V *>(stg + oB + 4096 * r) = B[r];
+            });
+          }
+        } else if (sA < K::W) { // A in column 7, B carried into column 0
+          const int oA = rb + ((8 * sA) ^ sw);
+          const int o0 = rb + sw;
+          static_for<0, 4>([&](auto rIC) {
+            constexpr int r = decltype(rIC)::value;
+            *reinterpret_cast<V *>(stg + oA + 4096 * r) = A[r];
+            *reinterpret_cast<V *>(stg + o0 + 4096 * r) = c0[192 * r];
+            c0[192 * r] = B[r];
+          });
+        } else { // both carried: slots s0, s0 + 1 (columns s0, s0 + 1)
+          const int s0 = sA - K::W;
+          const int oa = rb + ((8 * s0) ^ sw);
+          const int ob = rb + ((8 * s0 + 8) ^ sw);
+          static_for<0, 4>([&](auto rIC) {
+            constexpr int r = decltype(rIC)::value;
+            *reinterpret_cast<V *>(stg + oa + 4096 * r) = c0[192 * r + s0];
+            *reinterpret_cast<V *>(stg + ob + 4096 * r) = c0[192 * r + s0 + 1];
+            c0[192 * r + s0] = A[r];
+            c0[192 * r + s0 + 1] = B[r];
+          });
+        }
+      };
+      stage(q1, i1, car1, d1, A1, B1);
+      stage(q2, i2, car2, d2, A2, B2);
+      if (t0) { // bin 1024 (outside the class boxes): Z[1024] mirrors itself
+        const V z = v[bitrev<8>(4)];
+        V *gp = p.out + c * p.o_cs + (int64_t)(L / 2) * p.o_rs + x0 + 2 * g;
+        gp[0] = V{z.x + z.x, 0.f};
+        gp[1] = V{z.y + z.y, 0.f};
+      }
+    } else {
+      // ------------- first or last tile of a run or channel: general stores
+      V *outc = p.out + c * p.o_cs + x0 + 2 * g;
+      const bool okA = x0 + 2 * g < p.S, okB = x0 + 2 * g + 1 < p.S;
+      const bool nobox = tl + 1 == p.tpc; // a channel's last tile: no boxes
+      // one bin (class q, row i, bin k) of this thread's two columns
+      auto put = [&](int q, int d, V *cr, int i, int k, V A, V B) {
+        const int sA = 2 * g + d; // staging column of A (B at sA + 1)
+        V *gp = outc + (int64_t)k * p.o_rs;
+        const bool dir = nobox || (first && d != 0);
+        if (sA + 1 < K::W) {
+          if (dir) {
+            if (okA)
+              gp[0] = A;
+            if (okB)
+              gp[1] = B;
+          } else if ((sA & 1) == 0) {
+            *reinterpret_cast<float4 *>(stg + stma_off(q, i, sA)) =
+                make_float4(A.x, A.y, B.x, B.y);
+          } else {
+            *reinterpret_cast<V *>(stg + stma_off(q, i, sA)) = A;
+            *reinterpret_cast<V *>(stg + stma_off(q, i, sA + 1)) = B;
+          }
+        } else if (sA < K::W) { // B is carried (slot 0)
+          if (dir) {
+            if (okA)
+              gp[0] = A;
+          } else {
+            *reinterpret_cast<V *>(stg + stma_off(q, i, sA)) = A;
+          }
+          if (!first) { // the previous tile's B of this thread
+            if (nobox)
+              gp[1 - K::W] = cr[i * 3];
+            else
+              *reinterpret_cast<V *>(stg + stma_off(q, i, 0)) = cr[i * 3];
+          }
+          if (last) {
+            if (okB)
+              gp[1] = B;
+          } else {
+            cr[i * 3] = B;
+          }
+        } else { // both carried (slots sA - 8, sA - 7)
+          const int s0 = sA - K::W;
+          if (!first) {
+            if (nobox) {
+              gp[-K::W] = cr[i * 3 + s0];
+              gp[1 - K::W] = cr[i * 3 + s0 + 1];
+            } else {
+              *reinterpret_cast<V *>(stg + stma_off(q, i, s0)) = cr[i * 3 + s0];
+              *reinterpret_cast<V *>(stg + stma_off(q, i, s0 + 1)) =
+                  cr[i * 3 + s0 + 1];
+            }
+          }
+          if (last) {
+            if (okA)
+              gp[0] = A;
+            if (okB)
+              gp[1] = B;
+          } else {
+            cr[i * 3 + s0] = A;
+            cr[i * 3 + s0 + 1] = B;
           }
         }
-        if (last) {
-          if (okA)
-            gp[0] = A;
-          if (okB)
-            gp[1] = B;
-        } else {
-          cr[i * 3 + s0] = A;
-          cr[i * 3 + s0 + 1] = B;
-        }
+      };
+      static_for<0, 4>([&](auto rIC) {
+        constexpr int r = decltype(rIC)::value;
+        put(q1, d1, car1, i1 + 64 * r, jb0 + 256 * r, A1[r], B1[r]);
+        put(q2, d2, car2, i2 + 64 * r, jb1 + 256 * r, A2[r], B2[r]);
+      });
+      if (t0) { // bin 1024 (outside the class boxes): Z[1024] mirrors itself
+        const V z = v[bitrev<8>(4)];
+        V *gp = outc + (int64_t)(L / 2) * p.o_rs;
+        if (okA)
+          gp[0] = V{z.x + z.x, 0.f};
+        if (okB)
+          gp[1] = V{z.y + z.y, 0.f};
       }
-    };
-    static_for<0, 4>([&](auto rIC) {
-      constexpr int r = decltype(rIC)::value;
-      put(q1, car1, i1 + 64 * r, jb0 + 256 * r, A1[r], B1[r]);
-      put(q2, car2, i2 + 64 * r, jb1 + 256 * r, A2[r], B2[r]);
-    });
-    if (t0) { // bin 1024 (outside the class boxes): Z[1024] mirrors itself
-      const V z = v[bitrev<8>(4)];
-      V *gp = outc + (int64_t)(L / 2) * p.o_rs;
-      if (okA)
-        gp[0] = V{z.x + z.x, 0.f};
-      if (okB)
-        gp[1] = V{z.y + z.y, 0.f};
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if constexpr (TW) {
