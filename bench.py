@@ -782,7 +782,7 @@ def run_ours(args, w):
 # the channel count: the traffic is per channel; output bytes still in L2 at
 # the end of the small capture are missing, so this is a lower bound).
 TRAFFIC = {
-    "stft": lambda C: (152_996_096 + 497_428_480) / 8 * C,
+    "stft": lambda C: (140_656_384 + 489_337_856) / 8 * C,
 }
 
 

@@ -9,7 +9,6 @@
 
 #include <cudaTypedefs.h>
 #include <algorithm>
-#include <cstdlib>
 #include <type_traits>
 
 namespace ib200 {
@@ -329,11 +328,11 @@ inline cudaError_t encode_stft_map(CUtensorMap *tm, const LaunchDesc &d, int m) 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int SH, bool TW>
+template <int SH>
 cudaError_t run_stft_tma_sh(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                             int64_t *launches) {
   using K = StftTma;
-  auto kern = stft_tma_kernel<SH, TW>;
+  auto kern = stft_tma_kernel<SH>;
   static const cudaError_t attr = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::SMEM);
   if (attr != cudaSuccess)
@@ -359,42 +358,28 @@ cudaError_t run_stft_tma_sh(const LaunchDesc &d, int num_sms, cudaStream_t strea
       return e;
   }
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.ntiles, num_sms));
-  kern<<<(unsigned)grid, K::nt(TW), K::SMEM, stream>>>(a, tm[0], tm[1], tm[2], tm[3]);
+  kern<<<(unsigned)grid, K::NT, K::SMEM, stream>>>(a, tm[0], tm[1], tm[2], tm[3]);
   if (launches)
     *launches += 1;
   return cudaGetLastError();
 }
 
-template <bool TW>
-cudaError_t run_stft_tma(const LaunchDesc &d, int num_sms, cudaStream_t stream,
-                         int64_t *launches) {
+inline cudaError_t run_stft_tma(const LaunchDesc &d, int num_sms,
+                                cudaStream_t stream, int64_t *launches) {
   const int sh = fast_shift<float, StftTma::L>(d.step);
   if (sh == 4)
-    return run_stft_tma_sh<4, TW>(d, num_sms, stream, launches);
+    return run_stft_tma_sh<4>(d, num_sms, stream, launches);
   if (sh == 8)
-    return run_stft_tma_sh<8, TW>(d, num_sms, stream, launches);
-  return run_stft_tma_sh<0, TW>(d, num_sms, stream, launches);
-}
-
-// EXPERIMENT: IB200_STFT_VARIANT=ws|tw|t0 (default t0)
-inline int stft_variant() {
-  static const int v = [] {
-    const char *e = getenv("IB200_STFT_VARIANT");
-    if (!e) return 2;
-    if (e[0] == 'w') return 0;
-    if (e[0] == 't' && e[1] == 'w') return 1;
-    return 2;
-  }();
-  return v;
+    return run_stft_tma_sh<8>(d, num_sms, stream, launches);
+  return run_stft_tma_sh<0>(d, num_sms, stream, launches);
 }
 
 template <typename T, int L>
 cudaError_t run_stft_fast(const LaunchDesc &d, int num_sms, cudaStream_t stream,
                           int64_t *launches) {
   if constexpr (std::is_same<T, float>::value && L == StftTma::L) {
-    if (stft_tma_eligible(d) && stft_variant() != 0)
-      return stft_variant() == 1 ? run_stft_tma<true>(d, num_sms, stream, launches)
-                                 : run_stft_tma<false>(d, num_sms, stream, launches);
+    if (stft_tma_eligible(d))
+      return run_stft_tma(d, num_sms, stream, launches);
   }
   if constexpr (stft_ws_mode<T, L>() > 0) {
     constexpr int E = values_per_thread<T>(L);
