@@ -84,6 +84,9 @@ __device__ __forceinline__ void stage_copy(T *dst, const T *src, int64_t n,
 #ifndef IB200_ACC_SHFL
 #define IB200_ACC_SHFL 1
 #endif
+#ifndef IB200_ACC_PF
+#define IB200_ACC_PF 1
+#endif
 template <typename T, int L, int E>
 __host__ __device__ constexpr bool acc_shfl(int mode, int twm) {
   return IB200_ACC_SHFL && mode == ACC_PSD && twm == 1 &&
@@ -94,6 +97,11 @@ __host__ __device__ constexpr bool acc_mirrored(int mode, int twm) {
   return IB200_ACC_MIR && mode != ACC_PSD && twm == 1 &&
          Plan<L, E>::passes() >= 2 &&
          E / Plan<L, E>::radix(Plan<L, E>::passes() - 1) >= 2;
+}
+
+template <typename T, int L, int E>
+__host__ __device__ constexpr bool acc_prefetch(int mode, int twm, bool stg) {
+  return IB200_ACC_PF && mode == ACC_CSD && !stg && acc_mirrored<T, L, E>(mode, twm);
 }
 
 template <typename T, int L, int E, int G, int SH, int TWM, int MODE, bool STG>
@@ -119,6 +127,12 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   constexpr int NSL = L / RL;
   constexpr int HB = E / RL / 2; // mirrored butterfly pairs per thread
   static_assert(!MIR || NB == E / 2 + 1, "mirrored bins: E/2 + Nyquist");
+  // PF (csd on the mirrored path, samples from global memory): the cross
+  // products accumulate in f32 for FL tasks and then into f64 totals kept in
+  // shared memory, and the registers this frees hold the next transform's
+  // samples, loaded during the current transform (y during x's, the next
+  // task's x during y's)
+  constexpr bool PF = acc_prefetch<T, L, E>(MODE, TWM, STG);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // welch: one transform buffer and a 2L staging span per group; csd and
   // coherence: x and y buffers, x and y staging spans.
@@ -130,6 +144,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   constexpr int TWROW = TWM == 2 ? TT::stride()
                                  : (TWM == 1 ? ThreadTw1<T, L, E>::stride() : 0);
   T *wsm = reinterpret_cast<T *>(tws + P * TWROW);                // [P][WS]
+  double *acc64 = reinterpret_cast<double *>(wsm + P * WS);      // PF: [2NB][NT]
   const int g = threadIdx.x / P;
   const int t = threadIdx.x - g * P;
   V *buf = bufs + g * NBUF * GS;
@@ -284,6 +299,117 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
         issue(task0 + g);
     }
 
+    if constexpr (PF) {
+      // f32 partials (FL tasks) over f64 totals in shared memory
+      T accp[2 * NB];
+#pragma unroll
+      for (int i = 0; i < 2 * NB; ++i) {
+        accp[i] = T(0);
+        acc64[i * NT + threadIdx.x] = 0.0;
+      }
+      // samples of one transform: a (E values) and b's own (the rest share
+      // a's registers through the overlap shift)
+      constexpr int NBO = [] {
+        int n = 0;
+        for (int e = 0; e < E; ++e)
+          if (!(SH > 0 && (e % R0) + SH < R0))
+            ++n;
+        return n;
+      }();
+      T ra[E], rb[NBO > 0 ? NBO : 1];
+      auto load_raw = [&](const T *src, int64_t task) {
+        const bool hb = (2 * task + 1) < p.S;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          ra[e] = __ldg(src + in_index<L, E, P>(0, e));
+        });
+        int j = 0;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          if constexpr (!(SH > 0 && (e % R0) + SH < R0)) {
+            rb[j] = hb ? __ldg(src + p.step + in_index<L, E, P>(0, e)) : T(0);
+            ++j;
+          }
+        });
+      };
+      auto form = [&](V(&v)[E], bool hb) {
+        int j = 0;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          const T w = wrow[e];
+          T b;
+          if constexpr (SH > 0 && (e % R0) + SH < R0)
+            b = ra[e + SH];
+          else
+            b = rb[j++];
+          v[e] = {ra[e] * w, hb ? b * w : T(0)};
+        });
+      };
+      auto soff = [&](int64_t task) { return (p.seg0 + 2 * task) * p.step + t; };
+      if (task0 + g < task1)
+        load_raw(xc + soff(task0 + g), task0 + g);
+      int nfl = 0;
+      for (int64_t task = task0 + g; task < task1; task += G) {
+        const bool hasb = (2 * task + 1) < p.S;
+        V v[E];
+        form(v, hasb);                       // x
+        load_raw(yc + soff(task), task);     // y, during x's transform
+        fft(v, buf);
+        // park x's registers in this thread's column of buf: every read of
+        // buf by the transform ended at its last group barrier
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          buf[e * P + t] = v[e];
+        form(v, hasb);                       // y
+        if (task + G < task1)                // the next x, during y's transform
+          load_raw(xc + soff(task + G), task + G);
+        fft(v, buf2);
+        auto bin = [&](auto sIC, V xk, V xm, V yk, V ym) {
+          constexpr int sb = decltype(sIC)::value;
+          const T xar = xk.x + xm.x, xai = xk.y - xm.y;
+          const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
+          const T yar = yk.x + ym.x, yai = yk.y - ym.y;
+          const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
+          accp[2 * sb] += fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
+          accp[2 * sb + 1] +=
+              fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+        };
+        auto px = [&](int e) { return buf[e * P + t]; };
+        const bool j0 = t == 0; // butterflies 0 and NS/2 mirror themselves
+        static_for<0, HB>([&](auto hIC) {
+          constexpr int h = decltype(hIC)::value;
+          static_for<0, RL / 2>([&](auto rIC) {
+            constexpr int r = decltype(rIC)::value;
+            constexpr int ea = h * RL + bitrev<RL>(r);
+            constexpr int eam = (h + HB) * RL + bitrev<RL>(RL - 1 - r);
+            constexpr int eself = h * RL + bitrev<RL>((RL - r) % RL);
+            constexpr int ec = (h + HB) * RL + bitrev<RL>(r);
+            constexpr int ecm = h * RL + bitrev<RL>(RL - 1 - r);
+            const bool self = h == 0 && j0;
+            bin(std::integral_constant<int, h * RL + 2 * r>{}, px(ea),
+                px(self ? eself : eam), v[ea], self ? v[eself] : v[eam]);
+            bin(std::integral_constant<int, h * RL + 2 * r + 1>{}, px(ec),
+                px(self ? eam : ecm), v[ec], self ? v[eam] : v[ecm]);
+          });
+        });
+        if (j0) {
+          constexpr int en = bitrev<RL>(RL / 2);
+          bin(std::integral_constant<int, E / 2>{}, px(en), px(en), v[en], v[en]);
+        }
+        group_sync<G, P>(g); // the parked column is read before buf is reused
+        if (++nfl == FL) {
+#pragma unroll
+          for (int i = 0; i < 2 * NB; ++i) {
+            acc64[i * NT + threadIdx.x] += (double)accp[i];
+            accp[i] = T(0);
+          }
+          nfl = 0;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 2 * NB; ++i)
+        acc[i] = acc64[i * NT + threadIdx.x] + (double)accp[i];
+    } else
     for (int64_t task = task0 + g; task < task1; task += G) {
       const bool hasb = (2 * task + 1) < p.S;
       const int64_t off = (p.seg0 + 2 * task) * p.step;

@@ -470,6 +470,8 @@ constexpr size_t acc_fast_smem(int G, int twm, bool stg, int mode) {
     b += (size_t)P * ThreadTw<T, L, E>::stride() * 2 * sizeof(T);
   else if (twm == 1)
     b += (size_t)P * ThreadTw1<T, L, E>::stride() * 2 * sizeof(T);
+  if (acc_prefetch<T, L, E>(mode, twm, stg)) // f64 totals, 2 (E/2 + 1) a thread
+    b += (size_t)G * P * 2 * (E / 2 + 1) * sizeof(double);
   return b;
 }
 
@@ -484,7 +486,9 @@ constexpr AccShape acc_fast_shape() {
   constexpr int MAXT = MODE == ACC_COH ? 256 : 512;
   constexpr int E = values_per_thread<T>(L);
   constexpr int P = L / E;
-  constexpr size_t budget = 220 * 1024;
+  // the prefetching csd shape holds its f64 totals in shared memory too
+  constexpr size_t budget =
+      acc_prefetch<T, L, E>(MODE, 1, STG) ? 227 * 1024 : 220 * 1024;
   int g = 8;
   while (g > 1 && g * P > MAXT)
     --g;
