@@ -37,6 +37,24 @@ template <typename V> __device__ __forceinline__ V vadd(V a, V b) {
 template <typename V> __device__ __forceinline__ V vsub(V a, V b) {
   return {a.x - b.x, a.y - b.y};
 }
+// PK: f32 complex adds and subtracts as one packed two-lane instruction each
+// (sm_100 FADD2 / FFMA2: half the issue slots of two scalar ones, each lane
+// rounded as the scalar operation; a - b is fma(b, -1, a), exact before its
+// one rounding).  The butterfly networks of the transforms are mostly these.
+// Whether it pays depends on the kernel (measured: csd 5.27 -> 4.85 ms, the
+// stft kernel 1.56 -> 1.62 ms), so each kernel chooses.
+template <bool PK, typename V> __device__ __forceinline__ V vadd_k(V a, V b) {
+  if constexpr (PK && std::is_same<V, float2>::value)
+    return __fadd2_rn(a, b);
+  else
+    return vadd(a, b);
+}
+template <bool PK, typename V> __device__ __forceinline__ V vsub_k(V a, V b) {
+  if constexpr (PK && std::is_same<V, float2>::value)
+    return __ffma2_rn(b, make_float2(-1.f, -1.f), a);
+  else
+    return vsub(a, b);
+}
 // a * b (complex)
 template <typename V> __device__ __forceinline__ V vmul(V a, V b) {
   return {fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x)};
@@ -150,7 +168,7 @@ template <int R> __host__ __device__ constexpr int bitrev(int v) {
 // In-register R-point forward DFT: natural-order input, output in
 // bit-reversed register order (a[i] = X[bitrev(i)]); consumers index with
 // bitrev<R>() at compile time instead of moving registers.
-template <typename T, int R, typename V>
+template <typename T, int R, bool PK = false, typename V>
 __device__ __forceinline__ void dft_reg(V *a) {
   static_assert(R >= 1 && R <= 32 && (R & (R - 1)) == 0, "radix");
   if constexpr (R > 1) {
@@ -165,8 +183,8 @@ __device__ __forceinline__ void dft_reg(V *a) {
           static_for<0, H>([&](auto iIC) {
             constexpr int i = decltype(iIC)::value;
             V u = a[blk + i], w = a[blk + i + H];
-            a[blk + i] = vadd(u, w);
-            a[blk + i + H] = mul_w32<T, i * (32 / (2 * H))>(vsub(u, w));
+            a[blk + i] = vadd_k<PK>(u, w);
+            a[blk + i + H] = mul_w32<T, i * (32 / (2 * H))>(vsub_k<PK>(u, w));
           });
         });
       }
@@ -511,7 +529,7 @@ __device__ __forceinline__ void fill_thread_w1(V *rows, const V *tw, int tid,
   });
 }
 
-template <typename T, int L, int E, int P, int PASS, typename V>
+template <typename T, int L, int E, int P, int PASS, bool PK = false, typename V>
 __device__ __forceinline__ void pass_compute_w1(V *v, const V *row1) {
   using PL = Plan<L, E>;
   using TT = ThreadTw1<T, L, E>;
@@ -522,7 +540,7 @@ __device__ __forceinline__ void pass_compute_w1(V *v, const V *row1) {
     constexpr int b = decltype(bIC)::value;
     if constexpr (NS > 1)
       apply_twiddles<R>(v + b * R, row1[TT::offset(PASS) + b]);
-    dft_reg<T, R>(v + b * R);
+    dft_reg<T, R, PK>(v + b * R);
   });
 }
 
@@ -549,7 +567,7 @@ __device__ __forceinline__ void fft_group_w1(V *v, V *buf, int t, int g,
 // rows must come from fill_thread_w1<..., true>).  The transform is left in
 // registers: element r of butterfly b, bin pair_j(t, b) + r*L/R, at
 // v[b*R + bitrev(r)].
-template <typename T, int L, int E, int P, int G, typename V>
+template <typename T, int L, int E, int P, int G, bool PK = false, typename V>
 __device__ __forceinline__ void fft_group_w1_pairs(V *v, V *buf, int t, int g,
                                                    const V *row1) {
   using PL = Plan<L, E>;
@@ -576,7 +594,7 @@ __device__ __forceinline__ void fft_group_w1_pairs(V *v, V *buf, int t, int g,
       });
       group_sync<G, P>(g);
     }
-    pass_compute_w1<T, L, E, P, p>(v, row1);
+    pass_compute_w1<T, L, E, P, p, PK>(v, row1);
     if constexpr (p + 1 < NP) {
       pass_store<L, E, P, p>(v, buf, t);
       group_sync<G, P>(g);
