@@ -108,6 +108,17 @@ template <typename T, int L, int E>
 __host__ __device__ constexpr bool acc_prefetch(int mode, int twm, bool stg) {
   return IB200_ACC_PF && mode == ACC_CSD && !stg && acc_mirrored<T, L, E>(mode, twm);
 }
+// PFW: the same for welch on the shuffle-last-pass shape (f32 nperseg 8192):
+// the next task's samples in registers instead of cp.async staging (two CTA
+// barriers a transform fewer), f64 totals in shared memory.
+#ifndef IB200_ACC_PFW
+#define IB200_ACC_PFW 1
+#endif
+template <typename T, int L, int E>
+__host__ __device__ constexpr bool acc_prefetch_psd(int mode, int twm, bool stg) {
+  return IB200_ACC_PFW && mode == ACC_PSD && !stg && sizeof(T) == 4 &&
+         acc_shfl<T, L, E>(mode, twm);
+}
 
 template <typename T, int L, int E, int G, int SH, int TWM, int MODE, bool STG>
 __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
@@ -138,6 +149,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   // samples, loaded during the current transform (y during x's, the next
   // task's x during y's)
   constexpr bool PF = acc_prefetch<T, L, E>(MODE, TWM, STG);
+  constexpr bool PFW = acc_prefetch_psd<T, L, E>(MODE, TWM, STG);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // welch: one transform buffer and a 2L staging span per group; csd and
   // coherence: x and y buffers, x and y staging spans.
@@ -149,7 +161,7 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   constexpr int TWROW = TWM == 2 ? TT::stride()
                                  : (TWM == 1 ? ThreadTw1<T, L, E>::stride() : 0);
   T *wsm = reinterpret_cast<T *>(tws + P * TWROW);                // [P][WS]
-  double *acc64 = reinterpret_cast<double *>(wsm + P * WS);      // PF: [2NB][NT]
+  double *acc64 = reinterpret_cast<double *>(wsm + P * WS); // PF: [2NB][NT], PFW: [E][NT]
   const int g = threadIdx.x / P;
   const int t = threadIdx.x - g * P;
   V *buf = bufs + g * NBUF * GS;
@@ -304,7 +316,74 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
         issue(task0 + g);
     }
 
-    if constexpr (PF) {
+    if constexpr (PFW) {
+      // welch: f32 partials (FL tasks) over f64 totals in shared memory, the
+      // next task's samples loaded into registers during this transform
+#pragma unroll
+      for (int i = 0; i < E; ++i)
+        acc64[i * NT + threadIdx.x] = 0.0;
+      constexpr int NBO = [] {
+        int n = 0;
+        for (int e = 0; e < E; ++e)
+          if (!(SH > 0 && (e % R0) + SH < R0))
+            ++n;
+        return n;
+      }();
+      T ra[E], rb[NBO > 0 ? NBO : 1];
+      auto load_raw = [&](const T *src, int64_t task) {
+        const bool hb = (2 * task + 1) < p.S;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          ra[e] = __ldg(src + in_index<L, E, P>(0, e));
+        });
+        int j = 0;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          if constexpr (!(SH > 0 && (e % R0) + SH < R0)) {
+            rb[j] = hb ? __ldg(src + p.step + in_index<L, E, P>(0, e)) : T(0);
+            ++j;
+          }
+        });
+      };
+      auto soff = [&](int64_t task) { return (p.seg0 + 2 * task) * p.step + t; };
+      if (task0 + g < task1)
+        load_raw(xc + soff(task0 + g), task0 + g);
+      int nfl = 0;
+      for (int64_t task = task0 + g; task < task1; task += G) {
+        const bool hasb = (2 * task + 1) < p.S;
+        V v[E];
+        int j = 0;
+        static_for<0, E>([&](auto eIC) {
+          constexpr int e = decltype(eIC)::value;
+          const T w = wreg[WREG ? e : 0];
+          T b;
+          if constexpr (SH > 0 && (e % R0) + SH < R0)
+            b = ra[e + SH];
+          else
+            b = rb[j++];
+          v[e] = {ra[e] * w, hasb ? b * w : T(0)};
+        });
+        if (task + G < task1)
+          load_raw(xc + soff(task + G), task + G);
+        fft(v, buf);
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          accf[e] = fma(v[e].x, v[e].x, fma(v[e].y, v[e].y, accf[e]));
+        if (++nfl == FL) {
+#pragma unroll
+          for (int i = 0; i < E; ++i) {
+            acc64[i * NT + threadIdx.x] += (double)accf[i];
+            accf[i] = T(0);
+          }
+          nfl = 0;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        acc[i] = acc64[i * NT + threadIdx.x] + (double)accf[i];
+        accf[i] = T(0); // already folded in
+      }
+    } else if constexpr (PF) {
       // f32 partials (FL tasks) over f64 totals in shared memory
       T accp[2 * NB];
 #pragma unroll

@@ -472,6 +472,8 @@ constexpr size_t acc_fast_smem(int G, int twm, bool stg, int mode) {
     b += (size_t)P * ThreadTw1<T, L, E>::stride() * 2 * sizeof(T);
   if (acc_prefetch<T, L, E>(mode, twm, stg)) // f64 totals, 2 (E/2 + 1) a thread
     b += (size_t)G * P * 2 * (E / 2 + 1) * sizeof(double);
+  if (acc_prefetch_psd<T, L, E>(mode, twm, stg)) // f64 totals, E a thread
+    b += (size_t)G * P * E * sizeof(double);
   return b;
 }
 
@@ -591,7 +593,12 @@ cudaError_t run_accum_fast_pick(const LaunchDesc &d, void *scratch, int num_sms,
                                 cudaStream_t stream, int64_t *launches) {
   constexpr AccShape S0 = acc_fast_shape<T, L, false, MODE>();
   constexpr AccShape S1 = acc_fast_shape<T, L, true, MODE>();
-  if constexpr (S1.G > 0 && S1.G >= S0.G) {
+  constexpr int E = values_per_thread<T>(L);
+  if constexpr (S0.G > 0 && acc_prefetch_psd<T, L, E>(MODE, S0.twm, false)) {
+    // welch with the register prefetch: no staging
+    return run_accum_fast_sh<T, L, MODE, SH, false>(d, scratch, num_sms, stream,
+                                                    launches);
+  } else if constexpr (S1.G > 0 && S1.G >= S0.G) {
     if (segments_aligned16<T, MODE>(d, L)) {
       const int b1 = acc_fast_blocks_per_sm<T, L, MODE, SH, true>();
       const int b0 = acc_fast_blocks_per_sm<T, L, MODE, SH, false>();
