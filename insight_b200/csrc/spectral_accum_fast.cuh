@@ -448,15 +448,14 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
         if (task + G < task1)                // the next x, during y's transform
           load_raw(xc + soff(task + G), task + G);
         fft(v, buf2);
+        // 4 (conj(Xa) Ya + conj(Xb) Yb) = 2 (conj(Zx[k]) Zy[k] +
+        // Zx[L-k] conj(Zy[L-k])): the segment spectra need not be unpacked
         auto bin = [&](auto sIC, V xk, V xm, V yk, V ym) {
           constexpr int sb = decltype(sIC)::value;
-          const T xar = xk.x + xm.x, xai = xk.y - xm.y;
-          const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
-          const T yar = yk.x + ym.x, yai = yk.y - ym.y;
-          const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
-          accp[2 * sb] += fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
-          accp[2 * sb + 1] +=
-              fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+          const T re = fma(xk.x, yk.x, fma(xk.y, yk.y, fma(xm.x, ym.x, xm.y * ym.y)));
+          const T im = fma(xk.x, yk.y, fma(-xk.y, yk.x, fma(xm.y, ym.x, -xm.x * ym.y)));
+          accp[2 * sb] = fma(T(2), re, accp[2 * sb]);
+          accp[2 * sb + 1] = fma(T(2), im, accp[2 * sb + 1]);
         };
         auto px = [&](int e) { return buf[e * P + t]; };
         const bool j0 = t == 0; // butterflies 0 and NS/2 mirror themselves
@@ -530,21 +529,21 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
         fft(v, buf2);
         // Zx = Xa + i Xb, Zy = Ya + i Yb: as in the staged epilogue below,
         // from registers (y) and the parked column (x)
+        // 4 (conj(Xa) Ya + conj(Xb) Yb) = 2 (conj(Zx[k]) Zy[k] +
+        // Zx[L-k] conj(Zy[L-k])) and 4 (|Xa|^2 + |Xb|^2) =
+        // 2 (|Zx[k]|^2 + |Zx[L-k]|^2): the segment spectra need not be
+        // unpacked
         auto bin = [&](auto sIC, V xk, V xm, V yk, V ym) {
           constexpr int s = decltype(sIC)::value;
-          const T xar = xk.x + xm.x, xai = xk.y - xm.y;
-          const T xbr = xk.y + xm.y, xbi = xm.x - xk.x;
-          const T yar = yk.x + ym.x, yai = yk.y - ym.y;
-          const T ybr = yk.y + ym.y, ybi = ym.x - yk.x;
-          const T re = fma(xar, yar, fma(xai, yai, fma(xbr, ybr, xbi * ybi)));
+          const T re = T(2) * fma(xk.x, yk.x, fma(xk.y, yk.y, fma(xm.x, ym.x, xm.y * ym.y)));
           if constexpr (MODE == ACC_COH) {
-            acc[3 * s] +=
-                (double)fma(xar, xar, fma(xai, xai, fma(xbr, xbr, xbi * xbi)));
-            acc[3 * s + 1] +=
-                (double)fma(yar, yar, fma(yai, yai, fma(ybr, ybr, ybi * ybi)));
+            acc[3 * s] += (double)(T(2) * fma(xk.x, xk.x, fma(xk.y, xk.y,
+                                                 fma(xm.x, xm.x, xm.y * xm.y))));
+            acc[3 * s + 1] += (double)(T(2) * fma(yk.x, yk.x, fma(yk.y, yk.y,
+                                                     fma(ym.x, ym.x, ym.y * ym.y))));
             acc[3 * s + 2] += (double)re;
           } else {
-            const T im = fma(xar, yai, fma(-xai, yar, fma(xbr, ybi, -xbi * ybr)));
+            const T im = T(2) * fma(xk.x, yk.y, fma(-xk.y, yk.x, fma(xm.y, ym.x, -xm.x * ym.y)));
             acc[2 * s] += (double)re;
             acc[2 * s + 1] += (double)im;
           }
