@@ -114,6 +114,9 @@ __host__ __device__ constexpr bool acc_prefetch(int mode, int twm, bool stg) {
 #ifndef IB200_ACC_PFW
 #define IB200_ACC_PFW 1
 #endif
+#ifndef IB200_ACC_L2P
+#define IB200_ACC_L2P 1
+#endif
 template <typename T, int L, int E>
 __host__ __device__ constexpr bool acc_prefetch_psd(int mode, int twm, bool stg) {
   return IB200_ACC_PFW && mode == ACC_PSD && !stg && sizeof(T) == 4 &&
@@ -150,6 +153,10 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
   // task's x during y's)
   constexpr bool PF = acc_prefetch<T, L, E>(MODE, TWM, STG);
   constexpr bool PFW = acc_prefetch_psd<T, L, E>(MODE, TWM, STG);
+  // L2P (f64 welch, samples from global memory): the next task's span is
+  // prefetched into L2 by one bulk prefetch a group and task
+  constexpr bool L2P = IB200_ACC_L2P && MODE == ACC_PSD && !STG && !PFW &&
+                       sizeof(T) == 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // welch: one transform buffer and a 2L staging span per group; csd and
   // coherence: x and y buffers, x and y staging spans.
@@ -501,6 +508,21 @@ __global__ void __launch_bounds__(G *(L / E), MODE == ACC_COH ? 2 : 1)
       if constexpr (STG) {
         cp_async_wait_all();
         group_sync<G, P>(g); // every thread's copies of this task landed
+      }
+      if constexpr (L2P) {
+        // the group's next task span [off', off' + step + L) (just L without
+        // its segment b) into L2 while this task's samples are used
+        if (t == 0 && task + G < task1) {
+          const int64_t tn = task + G;
+          const int64_t n = ((2 * tn + 1) < p.S ? p.step : 0) + L;
+          const T *src = xc + (p.seg0 + 2 * tn) * p.step;
+          const uint64_t bytes = (uint64_t)n * sizeof(T);
+          // a bulk prefetch needs a 16-byte aligned start and size
+          if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (bytes & 15) == 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src),
+                         "r"((unsigned)bytes)
+                         : "memory");
+        }
       }
       load_v(v, STG ? raw + t : xc + off + t, boff, hasb);
       if constexpr (MODE == ACC_PSD) {
